@@ -1,0 +1,150 @@
+"""Typed torch-facing calls of the seven kernels (the C ABI's typed entry
+points). Every call runs on the current torch CUDA stream and raises
+:class:`B200Error` on failure; there is no CPU or eager fallback.
+
+Layout notes: ``softmax``/``layernorm_fwd`` take row-major torch matrices
+(rows of contiguous elements = Julia columns). ``matmul``/``bmm`` take the
+Julia column-major storage as torch tensors: the Julia M x K matrix A is the
+torch tensor ``A_t`` of shape (K, M) (row stride = Julia column stride).
+``fmha`` takes row-major [B, H, S, D] tensors (= Julia (D, S, H, B)).
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+from .runtime import current_stream_handle
+
+_DT = {torch.float16: _lib.CTB_F16, torch.bfloat16: _lib.CTB_BF16, torch.float32: _lib.CTB_F32,
+       torch.float64: _lib.CTB_F64}
+
+
+def _st():
+    return current_stream_handle()
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise _lib.B200Error(-1, "expected CUDA tensors")
+
+
+def init(device=0):
+    _lib.call("ctb_init", int(device))
+
+
+def check_device():
+    """Synchronises and raises CTB_ERR_TIMEOUT if a bounded device wait gave up."""
+    _lib.call("ctb_check_device", _st())
+
+
+def fill_uniform(t, seed, lo=-1.0, hi=1.0, offset=0):
+    _need_cuda(t)
+    assert t.is_contiguous()
+    _lib.call("ctb_fill_uniform", t.data_ptr(), _DT[t.dtype], t.numel(), seed, offset, lo, hi,
+              _st())
+    return t
+
+
+def fill_normal(t, seed, mean=0.0, std=1.0, offset=0):
+    _need_cuda(t)
+    assert t.is_contiguous()
+    _lib.call("ctb_fill_normal", t.data_ptr(), _DT[t.dtype], t.numel(), seed, offset, mean, std,
+              _st())
+    return t
+
+
+def vadd(a, b, out=None):
+    _need_cuda(a, b)
+    if out is None:
+        out = torch.empty_like(a)
+    n = out.numel()
+    _lib.call("ctb_vadd", _DT[a.dtype], a.data_ptr(), b.data_ptr(), out.data_ptr(), n,
+              a.stride(0) if a.dim() else 1, b.stride(0) if b.dim() else 1,
+              out.stride(0) if out.dim() else 1, _st())
+    return out
+
+
+def rowsum(a, out=None, julia_colmajor=True):
+    """``sum(a; dims=2)``. With ``julia_colmajor`` the torch tensor (n, m) is the
+    Julia m x n array (stride (1, m)); otherwise a is a row-major (m, n)
+    matrix whose rows are summed."""
+    _need_cuda(a)
+    if julia_colmajor:
+        n, m = a.shape
+        si, sj = a.stride(1), a.stride(0)
+    else:
+        m, n = a.shape
+        si, sj = a.stride(0), a.stride(1)
+    if out is None:
+        out = torch.empty(m, dtype=torch.float32, device=a.device)
+    _lib.call("ctb_rowsum_f32", a.data_ptr(), out.data_ptr(), m, n, si, sj, out.stride(0), _st())
+    return out
+
+
+def softmax(x, out=None):
+    """Row-wise softmax of a (count, len) float32 tensor with unit inner stride."""
+    _need_cuda(x)
+    if out is None:
+        out = torch.empty_like(x)
+    count, length = x.shape
+    if x.stride(1) != 1 or out.stride(1) != 1:
+        raise _lib.B200Error(-4, "softmax: rows must be contiguous")
+    _lib.call("ctb_softmax_f32", x.data_ptr(), out.data_ptr(), length, count, x.stride(0),
+              out.stride(0), _st())
+    return out
+
+
+def layernorm_fwd(x, w, b, eps=1e-5, out=None, mean=None, rstd=None):
+    _need_cuda(x, w, b)
+    rows, n = x.shape
+    if x.stride(1) != 1:
+        raise _lib.B200Error(-4, "layernorm_fwd: rows must be contiguous")
+    out = torch.empty_like(x) if out is None else out
+    mean = torch.empty(rows, dtype=torch.float32, device=x.device) if mean is None else mean
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device) if rstd is None else rstd
+    _lib.call("ctb_layernorm_fwd_f32", x.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
+              mean.data_ptr(), rstd.data_ptr(), n, rows, x.stride(0), out.stride(0),
+              ctypes.c_float(eps), _st())
+    return out, mean, rstd
+
+
+def matmul(A_t, B_t, C_t=None):
+    """Julia C = A*B on column-major storage: A_t (K, M), B_t (N, K), C_t (N, M)."""
+    _need_cuda(A_t, B_t)
+    K, M = A_t.shape
+    N = B_t.shape[0]
+    if C_t is None:
+        C_t = torch.empty(N, M, dtype=A_t.dtype, device=A_t.device)
+    if A_t.dtype != torch.float16:
+        raise _lib.B200Error(-2, "matmul: typed entry is Float16")
+    _lib.call("ctb_gemm_f16", A_t.data_ptr(), B_t.data_ptr(), C_t.data_ptr(), M, N, K,
+              A_t.stride(0), B_t.stride(0), C_t.stride(0), _st())
+    return C_t
+
+
+def bmm(A_t, B_t, C_t=None):
+    """Batched Julia C_b = A_b*B_b: A_t (batch, K, M), B_t (batch, N, K), C_t (batch, N, M)."""
+    _need_cuda(A_t, B_t)
+    batch, K, M = A_t.shape
+    N = B_t.shape[1]
+    if C_t is None:
+        C_t = torch.empty(batch, N, M, dtype=A_t.dtype, device=A_t.device)
+    _lib.call("ctb_bgemm_f16", A_t.data_ptr(), B_t.data_ptr(), C_t.data_ptr(), M, N, K, batch,
+              A_t.stride(1), B_t.stride(1), C_t.stride(1), A_t.stride(0), B_t.stride(0),
+              C_t.stride(0), _st())
+    return C_t
+
+
+def fmha(q, k, v, scale, causal=False, out=None):
+    """Attention forward on contiguous [B, H, S, D] float16 tensors."""
+    _need_cuda(q, k, v)
+    for t in (q, k, v):
+        if not t.is_contiguous():
+            raise _lib.B200Error(-4, "fmha: tensors must be contiguous [B, H, S, D]")
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    out = torch.empty_like(q) if out is None else out
+    _lib.call("ctb_fmha_fwd_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, H,
+              Sq, Sk, D, ctypes.c_float(scale), 1 if causal else 0, _st())
+    return out
