@@ -272,7 +272,7 @@ static int gemm_f16_dispatch(const __half* A, const __half* B, __half* C, int M,
                              int64_t sB, int64_t sC, cudaStream_t st) {
   if (M < 0 || N < 0 || K < 0 || batch < 0) return set_error(CTB_ERR_SHAPE, "matmul: negative size");
   if (M == 0 || N == 0 || batch == 0) return CTB_OK;
-  if (!A || !B || !C) return set_error(CTB_ERR_ARG, "matmul: NULL pointer");
+  if (!C || (K > 0 && (!A || !B))) return set_error(CTB_ERR_ARG, "matmul: NULL pointer");
   if (lda < M || ldb < K || ldc < M)
     return set_error(CTB_ERR_LAYOUT, "matmul: leading dimension smaller than the column length");
   DeviceProps pr;

@@ -320,7 +320,7 @@ def test_registry_layernorm_bmm_fmha(dev):
                          [TileArray(torch.float32, 2)] + [TileArray(torch.float32, 1)] * 2 + [float, Constant(1024)])
     rows, n = 64, 1024
     X = N((rows, n), 1, dev)
-    W, Bv = N(n, 2, dev, 1.0, 0.1), N(n, 3, dev, 0.0, 0.1)
+    W, Bv = N(n, 2, dev, mean=1.0, std=0.1), N(n, 3, dev, std=0.1)
     Y, Mu, Rs = torch.empty_like(X), torch.empty(rows, device=dev), torch.empty(rows, device=dev)
     cb.launch(k, rows, X, W, Bv, Y, Mu, Rs, 1e-5)
     ry, rmu, rrs = O.layernorm_fwd(host(X), host(W), host(Bv))
@@ -349,5 +349,5 @@ def test_layout_errors_are_reported(dev):
     k = cb.triton_kernel("softmax", [TileArray(torch.float32, 2)] * 2)
     x = torch.zeros(8, 16, device=dev).t()  # Julia dim 1 not contiguous
     with pytest.raises(cb.B200Error) as e:
-        cb.launch(k, 1, torch.zeros(16, 8, device=dev).t(), x)
+        cb.launch(k, 1, torch.zeros(8, 16, device=dev).t(), x)
     assert e.value.status == "CTB_ERR_LAYOUT"
