@@ -1,14 +1,384 @@
-// Attention forward entry point. The tensor-core (tcgen05) kernel lives here;
-// shapes it does not take go to the CUDA-core kernel in fmha_simt.cu.
-#include "ctb_common.cuh"
+// Attention forward on the 5th-generation tensor cores (tcgen05), head_dim 128.
+//
+// cuTile example fmha.jl:20 (not vendored in the reference; report.html:2981
+// describes its 4-D tiles with head_dim contiguous): O = softmax(scale*QK^T
+// [+ causal mask]) V per (batch, head), Float16 Q/K/V/O, Float32 scores,
+// running max/sum and output accumulator.
+//
+// One CTA = one (batch*head, 256-query block), split into two 128-row query
+// tiles Q0/Q1 that ping-pong: while softmax warpgroup 0 turns S0 into P0,
+// the tensor core computes S1 (or P1*V), and vice versa.
+//   warps 0-3   softmax + epilogue for Q0 (TMEM lanes 0-127 of S0/O0)
+//   warps 4-7   softmax + epilogue for Q1
+//   warp  8     TMEM owner + MMA issuer (one thread)
+//   warp  9     TMA producer (one thread): Q once, then a 2-stage K / V ring
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// P_t (Float16, two per 32-bit column) overwrites the first 64 columns of S_t
+// once its row has been read, and feeds P_t*V as the TMEM A operand.
+// Scores are kept in log2 units (exp2 with scale*log2(e) folded in). The
+// running max is only moved when it grows by more than 8 (a factor 256), so
+// the O rescale in TMEM is rare; numerator and denominator always share the
+// same max, so the result is unchanged.
+// No cluster multicast anywhere; every wait is bounded.
+#include "sm100_ptx.cuh"
+
+#include <algorithm>
+#include <mutex>
 
 namespace ctb {
 
 int fmha_simt(const __half* Q, const __half* K, const __half* V, __half* O, int B, int H, int Sq,
               int Sk, int D, float scale, int causal, cudaStream_t st);
 
-int fmha_device_setup() { return CTB_OK; }
+namespace fmha {
+
+constexpr int D = 128;            // head dim handled by this kernel
+constexpr int BQ = 128;           // rows per query tile (UMMA M)
+constexpr int BKV = 128;          // keys per block (UMMA N of S, K of P*V)
+constexpr int THREADS = 320;
+constexpr int TILE_BYTES = BQ * D * 2;       // 32 KB: one 128 x 128 f16 tile
+constexpr int HALF_BYTES = TILE_BYTES / 2;   // one 64-wide (128-byte) TMA box
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
+constexpr unsigned ERR_BIT = 2u;
+
+struct Params {
+  __half* O;
+  int Sq, Sk, BH, n_qblk;
+  float scale_log2;
+  int causal;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// S_t = Q_t K^T for one key block: 8 MMAs of K = 16 over head_dim, Q and K
+// both K-major 128-byte-swizzled (two 64-wide boxes of 16 KB each).
+__device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sKa, int t,
+                                        int stage, uint64_t* s_full_t) {
+  using namespace sm100;
+  constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV, false, false);
+  const uint32_t qa = sQa + t * TILE_BYTES, ka = sKa + stage * TILE_BYTES;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+    mma_f16_ss(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
+               smem_desc_sw128(ka + off, 16, 1024), idesc_s, kk != 0);
+  }
+  mma_commit(s_full_t);
+}
+
+// O_t (+)= P_t V for one key block: P_t from TMEM (16 keys = 8 columns per
+// step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
+// 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
+__device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j) {
+  using namespace sm100;
+  constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
+  const uint32_t va = sVa + stage * TILE_BYTES;
+#pragma unroll
+  for (int kk = 0; kk < BKV / 16; ++kk)
+    mma_f16_ts(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
+               smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
+               (j > 0 || kk > 0) ? 1u : 0u);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fmha_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ,
+                            const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using namespace sm100;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;                        // Q0, Q1
+  uint8_t* sK = smem + 2 * TILE_BYTES;       // 2 stages
+  uint8_t* sV = smem + 4 * TILE_BYTES;       // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;  // [2]
+  uint64_t* o_full = bars + 13;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // Heaviest (latest, for causal) query blocks first.
+  const int lin = blockIdx.x;
+  const int qblk = p.n_qblk - 1 - lin / p.BH;
+  const int bh = lin % p.BH;
+  const int q0 = qblk * 2 * BQ;
+  int nb = (p.Sk + BKV - 1) / BKV;
+  if (p.causal) nb = min(nb, (q0 + 2 * BQ + BKV - 1) / BKV);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], BQ);
+      mbar_init(&o_full[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 8) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * BQ, bh);
+      for (int j = 0; j < nb && !*abort_flag; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait_bounded(&k_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
+        mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sK + s * TILE_BYTES + h * HALF_BYTES, &tmK, &k_full[s], h * 64, j * BKV, bh);
+        if (!mbar_wait_bounded(&v_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
+        mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sV + s * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[s], h * 64, j * BKV, bh);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, ERR_BIT);
+      if (ok) ok = mbar_wait_bounded(&k_full[0], 0, abort_flag, ERR_BIT);
+      if (ok) {
+        tc_fence_after();
+        issue_s(tmem, sQa, sKa, 0, 0, &s_full[0]);
+        issue_s(tmem, sQa, sKa, 1, 0, &s_full[1]);
+        mma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < nb; ++j) {
+        const int s = j & 1, sn = (j + 1) & 1;
+        const uint32_t ph = (j >> 1) & 1, phn = ((j + 1) >> 1) & 1;
+        const bool more = j + 1 < nb;
+        if (!(ok = mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT))) break;
+        if (!(ok = mbar_wait_bounded(&p_full[0], j & 1, abort_flag, ERR_BIT))) break;
+        tc_fence_after();
+        issue_pv(tmem, sVa, 0, s, j);
+        if (more) {
+          if (!(ok = mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT))) break;
+          tc_fence_after();
+          issue_s(tmem, sQa, sKa, 0, sn, &s_full[0]);
+        }
+        if (!(ok = mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT))) break;
+        tc_fence_after();
+        issue_pv(tmem, sVa, 1, s, j);
+        mma_commit(&v_empty[s]);
+        if (more) {
+          issue_s(tmem, sQa, sKa, 1, sn, &s_full[1]);
+          mma_commit(&k_empty[sn]);
+        }
+      }
+      mma_commit(&o_full[0]);
+      mma_commit(&o_full[1]);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int t = warp >> 2;        // query tile
+    const int quarter = warp & 3;   // TMEM lanes 32*quarter .. +31
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + t * BKV;
+    const uint32_t o_col = tmem + lane_off + 256 + t * D;
+    const int qrow = q0 + t * BQ + quarter * 32 + lane;
+    const float sl2 = p.scale_log2;
+    float m_use = -INFINITY, l = 0.f;
+    for (int j = 0; j < nb; ++j) {
+      if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag, ERR_BIT)) break;
+      tc_fence_after();
+      const int k0 = j * BKV;
+      const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > q0 + t * BQ);
+      // Pass 1: row max over the block (32 columns at a time).
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(s_col + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(r[i]);
+          if (need_mask) {
+            const int key = k0 + c * 32 + i;
+            if (key >= p.Sk || (p.causal && key > qrow)) v = -INFINITY;
+          }
+          mx = fmaxf(mx, v);
+        }
+      }
+      const float m_blk = mx * sl2;
+      float factor = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m_use = m_blk;
+      } else if (m_blk > m_use + RESCALE_THRESHOLD) {
+        factor = ex2(m_use - m_blk);
+        l *= factor;
+        m_use = m_blk;
+        rescale = true;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_t is stable here: P_t*V of block j-1 completed before S_t of block j.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_col + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st_32x32b_x32(o_col + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
+      // (-inf) - (-inf) would be NaN, so shift by 0 for them.
+      const float mref = (m_use == -INFINITY) ? 0.f : m_use;
+      // Pass 2: P = exp2(s*scale*log2e - m) as f16 pairs. Chunk c's 16 packed
+      // columns land in [16c, 16c+16), which pass 2 has already read.
+      float rsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t r[32], pk[16];
+        tmem_ld_32x32b_x32(s_col + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float a = __uint_as_float(r[2 * i]), b = __uint_as_float(r[2 * i + 1]);
+          if (need_mask) {
+            const int key = k0 + c * 32 + 2 * i;
+            if (key >= p.Sk || (p.causal && key > qrow)) a = -INFINITY;
+            if (key + 1 >= p.Sk || (p.causal && key + 1 > qrow)) b = -INFINITY;
+          }
+          a = ex2(fmaf(a, sl2, -mref));
+          b = ex2(fmaf(b, sl2, -mref));
+          rsum += a + b;
+          pk[i] = pack_half2(a, b);
+        }
+        tmem_st_32x32b_x16(s_col + c * 16, pk);
+      }
+      l += rsum;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (mbar_wait_bounded(&o_full[t], 0, abort_flag, ERR_BIT)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(o_col + c * 32, o);
+        tmem_ld_wait();
+        if (qrow < p.Sq) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+            dst[v] = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fmha
+
 int fmha_take_device_error(unsigned int* out) { return take_device_error(out); }
+
+static bool g_fmha_attr_done[64];
+static std::mutex g_fmha_mu;
+
+int fmha_device_setup() {
+  int dev = 0;
+  CTB_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_fmha_mu);
+  if (dev < 64 && g_fmha_attr_done[dev]) return CTB_OK;
+  CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_tcgen05_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      fmha::SMEM_BYTES));
+  if (dev < 64) g_fmha_attr_done[dev] = true;
+  return CTB_OK;
+}
+
+static int fmha_tc(const __half* Q, const __half* K, const __half* V, __half* O, int B, int H,
+                   int Sq, int Sk, float scale, int causal, cudaStream_t st) {
+  if (int rc = fmha_device_setup()) return rc;
+  const int BH = B * H;
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[3] = {64, 128, 1};
+  {
+    const uint64_t dims[3] = {(uint64_t)fmha::D, (uint64_t)Sq, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)fmha::D * 2, (uint64_t)Sq * fmha::D * 2};
+    if (int rc = encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, Q, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)fmha::D, (uint64_t)Sk, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)fmha::D * 2, (uint64_t)Sk * fmha::D * 2};
+    if (int rc = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, K, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, V, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  fmha::Params p;
+  p.O = O;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.BH = BH;
+  p.n_qblk = (Sq + 2 * fmha::BQ - 1) / (2 * fmha::BQ);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal;
+  const int64_t grid = (int64_t)p.n_qblk * BH;
+  if (grid > 0x7fffffff) return set_error(CTB_ERR_SHAPE, "fmha: too many query blocks");
+  fmha::fmha_fwd_tcgen05_kernel<<<(unsigned)grid, fmha::THREADS, fmha::SMEM_BYTES, st>>>(tq, tk,
+                                                                                         tv, p);
+  return launch_status("fmha_fwd_tcgen05_kernel");
+}
 
 }  // namespace ctb
 
@@ -22,8 +392,15 @@ extern "C" int ctb_fmha_fwd_f16(const void* Q, const void* K, const void* V, voi
     return set_error(CTB_ERR_SHAPE, "fmha: need batch, heads, seq_q >= 0 and seq_k, head_dim >= 1");
   if ((int64_t)batch * heads * seq_q == 0) return CTB_OK;
   if (!Q || !K || !V || !O) return set_error(CTB_ERR_ARG, "fmha: NULL pointer");
+  if (!(scale > 0.f)) return set_error(CTB_ERR_ARG, "fmha: scale must be positive");
   DeviceProps p;
   if (int rc = current_props(&p)) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  const bool tc_ok = head_dim == fmha::D && aligned16(Q) && aligned16(K) && aligned16(V) &&
+                     aligned16(O) && (int64_t)batch * heads <= 0x7fffffff;
+  if (tc_ok)
+    return fmha_tc((const __half*)Q, (const __half*)K, (const __half*)V, (__half*)O, batch, heads,
+                   seq_q, seq_k, scale, causal ? 1 : 0, st);
   return fmha_simt((const __half*)Q, (const __half*)K, (const __half*)V, (__half*)O, batch, heads,
-                   seq_q, seq_k, head_dim, scale, causal, static_cast<cudaStream_t>(stream));
+                   seq_q, seq_k, head_dim, scale, causal ? 1 : 0, st);
 }
