@@ -94,7 +94,7 @@ def load_traffic():
 class Case:
     """Inputs/outputs of one workload on the device plus the launch closure."""
 
-    def __init__(self, name, dev, rank):
+    def __init__(self, name, dev, rank, small=False):
         import torch
         from cutile_b200 import ops
 
@@ -107,7 +107,7 @@ class Case:
             self.run = lambda: ops.softmax(x, y)
             self.inputs, self.outputs = [x], [y]
         elif name == "vadd":
-            n = 1 << 28
+            n = (1 << 26) if small else (1 << 28)
             a = ops.fill_uniform(T.empty(n, device=dev), seed)
             b = ops.fill_uniform(T.empty(n, device=dev), seed + 1)
             c = T.empty_like(a)
@@ -140,7 +140,7 @@ class Case:
             self.run = lambda: ops.bmm(A, B, C)
             self.inputs, self.outputs = [A, B], [C]
         elif name in ("fmha", "fmha_causal"):
-            shape = (8, 32, 8192, 128)
+            shape = (1, 8, 8192, 128) if small else (8, 32, 8192, 128)
             q = ops.fill_normal(T.empty(shape, dtype=T.float16, device=dev), seed)
             k = ops.fill_normal(T.empty(shape, dtype=T.float16, device=dev), seed + 1)
             v = ops.fill_normal(T.empty(shape, dtype=T.float16, device=dev), seed + 2)
@@ -505,6 +505,26 @@ def run_ours(args):
     return 0
 
 
+def run_profile(args):
+    """Runs W warm-up launches and K launches of one workload, nothing else:
+    the command under ncu captures (`--profile NAME`, small inputs for vadd
+    and fmha so that a multi-pass capture stays a few GB and seconds)."""
+    import torch
+
+    from cutile_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ops.init(0)
+    case = Case(args.profile, dev, 0, small=True)
+    for _ in range(args.warmup + args.steps):
+        case.run()
+    torch.cuda.synchronize()
+    ops.check_device()
+    print(f"profile case {args.profile}: {args.warmup} + {args.steps} launches ok")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,8 +538,12 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU work for the headline cpu_baseline")
     ap.add_argument("--ref-budget", type=float, default=15.0)
+    ap.add_argument("--profile", default=None, choices=list(WORKLOADS),
+                    help="launch-only mode for ncu captures")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require >= 3 warm-up steps
+    if args.profile:
+        return run_profile(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -8,13 +8,15 @@
 // One CTA = one (batch*head, 256-query block), split into two 128-row query
 // tiles Q0/Q1 that ping-pong: while softmax warpgroup 0 turns S0 into P0,
 // the tensor core computes S1 (or P1*V), and vice versa.
-//   warps 0-3   softmax + epilogue for Q0 (TMEM lanes 0-127 of S0/O0)
-//   warps 4-7   softmax + epilogue for Q1
-//   warp  8     TMEM owner + MMA issuer (one thread)
-//   warp  9     TMA producer (one thread): Q once, then a 2-stage K / V ring
+//   warps 0-7   softmax + epilogue for Q0: a score row is split between two
+//               threads (64 columns each), warp w reads TMEM lanes 32*(w%4)
+//   warps 8-15  softmax + epilogue for Q1
+//   warp  16    TMEM owner + MMA issuer (one thread)
+//   warp  17    TMA producer (one thread): Q once, then a 2-stage K / V ring
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
-// P_t (Float16, two per 32-bit column) overwrites the first 64 columns of S_t
-// once its row has been read, and feeds P_t*V as the TMEM A operand.
+// P_t (Float16, two per 32-bit column) overwrites S_t columns 0-31 (keys
+// 0-63) and 64-95 (keys 64-127) once those scores have been read, and feeds
+// P_t*V as the TMEM A operand.
 // Scores are kept in log2 units (exp2 with scale*log2(e) folded in). The
 // running max is only moved when it grows by more than 8 (a factor 256), so
 // the O rescale in TMEM is rare; numerator and denominator always share the
@@ -35,10 +37,13 @@ namespace fmha {
 constexpr int D = 128;            // head dim handled by this kernel
 constexpr int BQ = 128;           // rows per query tile (UMMA M)
 constexpr int BKV = 128;          // keys per block (UMMA N of S, K of P*V)
-constexpr int THREADS = 320;
+constexpr int SM_THREADS_PER_TILE = 256;      // 8 softmax warps per query tile
+constexpr int MMA_WARP = 16, TMA_WARP = 17;
+constexpr int THREADS = 18 * 32;
 constexpr int TILE_BYTES = BQ * D * 2;       // 32 KB: one 128 x 128 f16 tile
 constexpr int HALF_BYTES = TILE_BYTES / 2;   // one 64-wide (128-byte) TMA box
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr int XCHG_BYTES = 2 * 2 * BQ * 4;    // per-row partial max / sum exchange
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + XCHG_BYTES + 1024 + 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 constexpr unsigned ERR_BIT = 2u;
 
@@ -60,6 +65,63 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ---- paired fp32 arithmetic (sm_100 f32x2 instructions) -----------------------
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe, x in [-126, 126]: Cody-Waite split
+// x = j + f with j = round(x) (1.5*2^23 rounding shifter) and f in
+// [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted here for minimum
+// relative error on [-0.5, 0.5] (max 7.5e-5, below Float16's half ulp);
+// 2^j added to the exponent field. Offloads the MUFU ex2 unit.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  const uint64_t shifter = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t t = f2_add(x, shifter);
+  const uint64_t f = f2_sub(x, f2_sub(t, shifter));
+  uint64_t p = f2_fma(f2_pack(0.05517146f, 0.05517146f), f, f2_pack(0.24261075f, 0.24261075f));
+  p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+  p = f2_fma(p, f, f2_pack(0.9999281f, 0.9999281f));
+  float pa, pb, ta, tb;
+  f2_unpack(p, pa, pb);
+  f2_unpack(t, ta, tb);
+  const float ra = __int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23));
+  const float rb = __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23));
+  return f2_pack(ra, rb);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Pairs of P evaluated with exp2_poly2 instead of MUFU ex2: one in EMU_EVERY.
+constexpr int EMU_EVERY = 4;
+
 // S_t = Q_t K^T for one key block: 8 MMAs of K = 16 over head_dim, Q and K
 // both K-major 128-byte-swizzled (two 64-wide boxes of 16 KB each).
 __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sKa, int t,
@@ -76,8 +138,8 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
   mma_commit(s_full_t);
 }
 
-// O_t (+)= P_t V for one key block: P_t from TMEM (16 keys = 8 columns per
-// step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
+// O_t (+)= P_t V for one key block: P_t from TMEM (keys 0-63 packed in S_t
+// columns 0-31, keys 64-127 in columns 64-95; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
 // 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
 __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j) {
   using namespace sm100;
@@ -85,7 +147,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
   const uint32_t va = sVa + stage * TILE_BYTES;
 #pragma unroll
   for (int kk = 0; kk < BKV / 16; ++kk)
-    mma_f16_ts(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
+    mma_f16_ts(tmem + 256 + t * D, tmem + t * BKV + (kk >> 2) * 64 + (kk & 3) * 8,
                smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
                (j > 0 || kk > 0) ? 1u : 0u);
 }
@@ -101,7 +163,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sQ = smem;                        // Q0, Q1
   uint8_t* sK = smem + 2 * TILE_BYTES;       // 2 stages
   uint8_t* sV = smem + 4 * TILE_BYTES;       // 2 stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES);
+  float* xchg = reinterpret_cast<float*>(smem + 6 * TILE_BYTES);  // [2 tiles][2 halves][128 rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES + XCHG_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -130,7 +193,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], BQ);
+      mbar_init(&p_full[i], SM_THREADS_PER_TILE);
       mbar_init(&o_full[i], 1);
     }
     *abort_flag = 0;
@@ -139,13 +202,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
-  if (warp == 8) tmem_alloc(tmem_slot, 512);
+  if (warp == MMA_WARP) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
@@ -165,7 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_3d(sV + s * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[s], h * 64, j * BKV, bh);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
@@ -177,6 +240,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         issue_s(tmem, sQa, sKa, 1, 0, &s_full[1]);
         mma_commit(&k_empty[0]);
       }
+      // Tensor-pipe order per key block j: PV0(j) S0(j+1) PV1(j) S1(j+1). The
+      // pipe executes one thread's MMAs in issue order, so S_t(j+1) never
+      // overwrites P_t(j) before P_t(j)*V has read it.
       for (int j = 0; ok && j < nb; ++j) {
         const int s = j & 1, sn = (j + 1) & 1;
         const uint32_t ph = (j >> 1) & 1, phn = ((j + 1) >> 1) & 1;
@@ -203,37 +269,54 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(&o_full[1]);
     }
   } else {
-    // ------------------------------------------------------------ softmax warpgroups
-    const int t = warp >> 2;        // query tile
-    const int quarter = warp & 3;   // TMEM lanes 32*quarter .. +31
+    // ------------------------------------------------------------ softmax warps
+    // Tile t has 8 warps; a score row is split between two threads (one per
+    // 64-column half) that exchange their partial max through shared memory.
+    const int t = warp / 8;
+    const int ww = warp % 8;
+    const int quarter = ww & 3;  // TMEM lanes 32*quarter .. +31 (warp id mod 4)
+    const int half = ww >> 2;    // score / output columns 64*half .. +63
+    const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_col = tmem + lane_off + t * BKV;
-    const uint32_t o_col = tmem + lane_off + 256 + t * D;
-    const int qrow = q0 + t * BQ + quarter * 32 + lane;
+    const uint32_t s_col = tmem + lane_off + t * BKV + half * 64;
+    // P of this half goes into the first 32 of its own 64 S columns.
+    const uint32_t p_col = s_col;
+    const uint32_t o_col = tmem + lane_off + 256 + t * D + half * 64;
+    float* my_x = xchg + (t * 2 + half) * BQ;
+    const float* other_x = xchg + (t * 2 + (half ^ 1)) * BQ;
+    const int qrow = q0 + t * BQ + row;
     const float sl2 = p.scale_log2;
     float m_use = -INFINITY, l = 0.f;
     for (int j = 0; j < nb; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag, ERR_BIT)) break;
       tc_fence_after();
-      const int k0 = j * BKV;
-      const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > q0 + t * BQ);
-      // Pass 1: row max over the block (32 columns at a time).
-      float mx = -INFINITY;
+      // Pass 1: this half's 64 scores -> partial row max, 32 columns at a time.
+      const int k0 = j * BKV + half * 64;
+      const bool need_mask =
+          (j * BKV + BKV > p.Sk) || (p.causal && j * BKV + BKV - 1 > q0 + t * BQ);
+      float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
+      for (int h = 0; h < 2; ++h) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(s_col + c * 32, r);
+        tmem_ld_32x32b_x32(s_col + h * 32, r);
         tmem_ld_wait();
+        if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(r[i]);
-          if (need_mask) {
-            const int key = k0 + c * 32 + i;
-            if (key >= p.Sk || (p.causal && key > qrow)) v = -INFINITY;
+          for (int i = 0; i < 32; ++i) {
+            const int key = k0 + h * 32 + i;
+            if (key >= p.Sk || (p.causal && key > qrow)) r[i] = __float_as_uint(-INFINITY);
           }
-          mx = fmaxf(mx, v);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          mxa = max3(mxa, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          mxb = max3(mxb, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
         }
       }
+      my_x[row] = fmaxf(mxa, mxb);
+      // Both threads of a row meet here to combine their partial maxima.
+      named_barrier_sync(1 + t, SM_THREADS_PER_TILE);
+      const float mx = fmaxf(my_x[row], other_x[row]);
       const float m_blk = mx * sl2;
       float factor = 1.f;
       bool rescale = false;
@@ -248,7 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (__any_sync(0xffffffffu, rescale)) {
         // O_t is stable here: P_t*V of block j-1 completed before S_t of block j.
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(o_col + c * 32, o);
           tmem_ld_wait();
@@ -256,46 +339,65 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
           tmem_st_32x32b_x32(o_col + c * 32, o);
         }
-        tmem_st_wait();
       }
       // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
       // (-inf) - (-inf) would be NaN, so shift by 0 for them.
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
-      // Pass 2: P = exp2(s*scale*log2e - m) as f16 pairs. Chunk c's 16 packed
-      // columns land in [16c, 16c+16), which pass 2 has already read.
-      float rsum = 0.f;
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), nm2 = f2_pack(-mref, -mref);
+      uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
+      // Pass 2 re-reads the scores 32 columns at a time (keeps registers low);
+      // chunk h's 16 packed P columns land in columns this thread already read.
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t r[32], pk[16];
-        tmem_ld_32x32b_x32(s_col + c * 32, r);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t rr[32], pk[16];
+        tmem_ld_32x32b_x32(s_col + h * 32, rr);
         tmem_ld_wait();
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = k0 + h * 32 + i;
+            if (key >= p.Sk || (p.causal && key > qrow)) rr[i] = __float_as_uint(-INFINITY);
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float a = __uint_as_float(r[2 * i]), b = __uint_as_float(r[2 * i + 1]);
-          if (need_mask) {
-            const int key = k0 + c * 32 + 2 * i;
-            if (key >= p.Sk || (p.causal && key > qrow)) a = -INFINITY;
-            if (key + 1 >= p.Sk || (p.causal && key + 1 > qrow)) b = -INFINITY;
-          }
-          a = ex2(fmaf(a, sl2, -mref));
-          b = ex2(fmaf(b, sl2, -mref));
-          rsum += a + b;
-          pk[i] = pack_half2(a, b);
+          const uint64_t x = f2_fma(f2_pack(__uint_as_float(rr[2 * i]),
+                                            __uint_as_float(rr[2 * i + 1])),
+                                    sl2x2, nm2);
+          float xa, xb;
+          f2_unpack(x, xa, xb);
+          uint64_t e;
+          if (!need_mask && (i % EMU_EVERY) == EMU_EVERY - 1)
+            e = exp2_poly2(f2_pack(fmaxf(xa, -126.f), fmaxf(xb, -126.f)));
+          else
+            e = f2_pack(ex2(xa), ex2(xb));
+          if (i & 1) acc1 = f2_add(acc1, e);
+          else acc0 = f2_add(acc0, e);
+          float ea, eb;
+          f2_unpack(e, ea, eb);
+          pk[i] = pack_half2(ea, eb);
         }
-        tmem_st_32x32b_x16(s_col + c * 16, pk);
+        tmem_st_32x32b_x16(p_col + h * 16, pk);
       }
-      l += rsum;
+      float s0, s1, s2, s3;
+      f2_unpack(acc0, s0, s1);
+      f2_unpack(acc1, s2, s3);
+      l += (s0 + s1) + (s2 + s3);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
     // ------------------------------------------------------------ epilogue
+    // Row sum = both halves' partial sums.
+    my_x[row] = l;
+    named_barrier_sync(1 + t, SM_THREADS_PER_TILE);
+    const float l_row = l + other_x[row];
     if (mbar_wait_bounded(&o_full[t], 0, abort_flag, ERR_BIT)) {
       tc_fence_after();
-      const float inv = 1.f / l;
-      __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D;
+      const float inv = 1.f / l_row;
+      __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D + half * 64;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(o_col + c * 32, o);
         tmem_ld_wait();
@@ -317,7 +419,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

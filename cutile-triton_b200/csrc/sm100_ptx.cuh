@@ -44,15 +44,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after ~`limit` polls (each try_wait may itself
-// suspend for a hardware-defined interval), flags `err_bit` in the device
-// error word and sets the CTA's abort flag so every role drains and exits.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait. The waiting thread is suspended inside try_wait (woken when
+// the phase completes, or after `suspend_ns`), so a waiting warp issues
+// almost nothing. After ~`limit_ns` of wall time (or when another role has
+// already given up) it flags `err_bit` in the device error word, sets the
+// CTA's abort flag so that every role drains and exits, and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag, unsigned err_bit,
-                                                  uint32_t limit = (1u << 26)) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && *abort_flag) return false;
+                                                  uint64_t limit_ns = 4000000000ull) {
+  if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > limit_ns) break;
   }
   *abort_flag = 1;
   flag_device_error(err_bit);
