@@ -36,15 +36,22 @@ def _needs(target, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force=False, verbose=False):
+def build(force=False, verbose=False, defines=(), lib=None, obj=None):
+    """Compiles every csrc/*.cu and links the library. `defines` (e.g.
+    ["CTB_FMHA_EMU_EVERY=2"]) override compile-time tunables; with them, pass
+    a separate `lib`/`obj` so the default build is left untouched."""
+    global OBJ, LIB
+    OBJ = obj or OBJ
+    LIB = lib or LIB
     os.makedirs(OBJ, exist_ok=True)
+    os.makedirs(os.path.dirname(LIB), exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")] + [HEADER]
     objs = []
     for src in sources():
-        obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
-        objs.append(obj)
-        if force or _needs(obj, [src] + headers):
-            cmd = [NVCC] + FLAGS + ["-c", src, "-o", obj]
+        o = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+        objs.append(o)
+        if force or _needs(o, [src] + headers):
+            cmd = [NVCC] + FLAGS + ["-D" + d for d in defines] + ["-c", src, "-o", o]
             if verbose:
                 cmd.insert(1, "-Xptxas=-v")
                 print(" ".join(cmd))

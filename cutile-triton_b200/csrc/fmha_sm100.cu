@@ -120,7 +120,10 @@ __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
 }
 
 // Pairs of P evaluated with exp2_poly2 instead of MUFU ex2: one in EMU_EVERY.
-constexpr int EMU_EVERY = 4;
+#ifndef CTB_FMHA_EMU_EVERY
+#define CTB_FMHA_EMU_EVERY 1000  // measured fastest on B200: no offload
+#endif
+constexpr int EMU_EVERY = CTB_FMHA_EMU_EVERY;
 
 // S_t = Q_t K^T for one key block: 8 MMAs of K = 16 over head_dim, Q and K
 // both K-major 128-byte-swizzled (two 64-wide boxes of 16 KB each).

@@ -68,13 +68,16 @@ __device__ __forceinline__ uint64_t global_ns() {
 // almost nothing. After ~`limit_ns` of wall time (or when another role has
 // already given up) it flags `err_bit` in the device error word, sets the
 // CTA's abort flag so that every role drains and exits, and returns false.
+#ifndef CTB_WAIT_SUSPEND_NS
+#define CTB_WAIT_SUSPEND_NS 20000u
+#endif
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag, unsigned err_bit,
                                                   uint64_t limit_ns = 4000000000ull) {
-  if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+  if (mbar_try_wait_sleep(bar, parity, CTB_WAIT_SUSPEND_NS)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, CTB_WAIT_SUSPEND_NS)) return true;
     if (*abort_flag) return false;
     if (global_ns() - t0 > limit_ns) break;
   }
