@@ -3,9 +3,8 @@
 // Design (B200, 148 SMs, HBM3e): every kernel moves its bytes once — 128-bit
 // loads with L1 no-allocate, evict-first stores, rows held in registers
 // between the reduction and the write-back — and reduces with warp shuffles
-// plus one shared-memory hop per CTA. Grids are persistent (a multiple of the
-// SM count x resident CTAs) where a CTA can keep per-column state (layernorm's
-// gamma/beta) in registers across rows.
+// plus one shared-memory hop per CTA. Row kernels size their grid to the
+// resident-CTA capacity (SM count x CTAs per SM) and stride over rows.
 #include "ctb_common.cuh"
 
 #include <algorithm>
@@ -368,17 +367,17 @@ static int launch_softmax(const float* x, float* y, int len, int count, int64_t 
 // layernorm forward (cuTile example layernorm.jl:27; definitions of mean,
 // biased variance and rstd as stated in include/cutile_b200.h)
 // =============================================================================
-// Persistent: gamma/beta stay in registers while the CTA walks its rows.
+// One row per CTA trip; gamma/beta are read through the read-only path at
+// write-back time (32 KB shared by every CTA of the SM, so they hit L1/L2),
+// which keeps registers low and lets more rows be in flight per SM.
 template <int THREADS, int NV, bool VEC>
-__global__ void __launch_bounds__(THREADS) layernorm_fwd_reg_kernel(
+__global__ void __launch_bounds__(THREADS, (THREADS >= 1024 ? 1 : 2048 / THREADS)) layernorm_fwd_reg_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
     float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int n, int rows,
     int64_t ldx, int64_t ldy, float eps) {
   __shared__ float red[THREADS / 32];
-  float wv[NV * 4], bv[NV * 4];
-  load_row<THREADS, NV, VEC>(w, n, 0.f, wv);
-  load_row<THREADS, NV, VEC>(b, n, 0.f, bv);
   const float inv_n = 1.0f / (float)n;
+  const int t = threadIdx.x;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     float v[NV * 4];
     load_row<THREADS, NV, VEC>(x + row * ldx, n, 0.f, v);
@@ -387,7 +386,6 @@ __global__ void __launch_bounds__(THREADS) layernorm_fwd_reg_kernel(
     for (int i = 0; i < NV * 4; ++i) s += v[i];
     const float mu = block_reduce<THREADS / 32, false>(s, red) * inv_n;
     float q = 0.f;
-    const int t = threadIdx.x;
 #pragma unroll
     for (int k = 0; k < NV; ++k)
 #pragma unroll
@@ -397,10 +395,26 @@ __global__ void __launch_bounds__(THREADS) layernorm_fwd_reg_kernel(
       }
     const float var = block_reduce<THREADS / 32, false>(q, red) * inv_n;
     const float rs = 1.0f / sqrtf(var + eps);
+    float* yr = y + row * ldy;
 #pragma unroll
-    for (int i = 0; i < NV * 4; ++i) v[i] = fmaf((v[i] - mu) * rs, wv[i], bv[i]);
-    store_row<THREADS, NV, VEC>(y + row * ldy, n, v);
-    if (threadIdx.x == 0) {
+    for (int k = 0; k < NV; ++k) {
+      const int idx0 = (k * THREADS + t) * 4;
+      if (VEC) {
+        if (idx0 < n) {
+          const float4 wq = __ldg(reinterpret_cast<const float4*>(w + idx0));
+          const float4 bq = __ldg(reinterpret_cast<const float4*>(b + idx0));
+          st_stream_f4(yr + idx0, make_float4(fmaf((v[4 * k] - mu) * rs, wq.x, bq.x),
+                                              fmaf((v[4 * k + 1] - mu) * rs, wq.y, bq.y),
+                                              fmaf((v[4 * k + 2] - mu) * rs, wq.z, bq.z),
+                                              fmaf((v[4 * k + 3] - mu) * rs, wq.w, bq.w)));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (idx0 + e < n) yr[idx0 + e] = fmaf((v[4 * k + e] - mu) * rs, __ldg(w + idx0 + e), __ldg(b + idx0 + e));
+      }
+    }
+    if (t == 0) {
       mean[row] = mu;
       rstd[row] = rs;
     }
@@ -470,8 +484,8 @@ static int launch_layernorm(const float* x, const float* w, const float* b, floa
                    aligned16(w) && aligned16(b);
   const int sm = p.sm_count;
   if (n <= 512) return layernorm_reg_launch<128, 1>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
-  if (n <= 2048) return layernorm_reg_launch<128, 4>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
-  if (n <= 4096) return layernorm_reg_launch<256, 4>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
+  if (n <= 2048) return layernorm_reg_launch<256, 2>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
+  if (n <= 4096) return layernorm_reg_launch<512, 2>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
   if (n <= 8192) return layernorm_reg_launch<512, 4>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
   if (n <= 16384) return layernorm_reg_launch<1024, 4>(x, w, b, y, mean, rstd, n, rows, ldx, ldy, eps, vec, sm, st);
   const int grid = std::min(rows, sm * 2);
