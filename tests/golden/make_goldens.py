@@ -1,0 +1,128 @@
+"""Generates the golden vectors in tests/golden/ by running the REFERENCE's own
+kernels on a GPU — test infrastructure.
+
+The kernels are the reference's TileTriton-emitted TTIR (vadd, rowsum) and
+its Python-Triton twin of the persistent column softmax, compiled for sm_100
+by oracle/build_ref.py into oracle/_ref/ (run that first, in a tree that has
+the reference). This script loads those cubins with the CUDA driver API,
+feeds them seeded inputs from the oracle's SplitMix64 generator (the same
+bits tests regenerate on the host), and writes:
+
+  ref_goldens.json  sha256 of every full output + metadata
+  ref_goldens.npz   rowsum outputs and sampled softmax columns
+
+Usage (on a machine with a B200):  python tests/golden/make_goldens.py [OUT_DIR]
+(OUT_DIR defaults to tests/golden/).
+"""
+import ctypes
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+REF = os.path.join(ROOT, "oracle", "_ref")
+
+# Shapes: the reference's own test cases (test/runtests.jl:39, 58, 120) and
+# the BASELINE vadd size.
+VADD_CASES = [(1_024_000, 1, 2), (999_999, 1, 2), (1 << 28, 20261201, 20261202)]
+ROWSUM_CASES = [(4096, 128, 3), (131072, 128, 5)]
+SOFTMAX_CASE = (1000, 2048, 4, 512)  # n_rows, n_cols, seed, grid
+SOFTMAX_COLS = list(range(8)) + list(range(8, 2048, 256))
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def main():
+    import torch
+    from cuda.bindings import driver as cu
+
+    from oracle import oracle as O
+
+    torch.cuda.init()
+    dev = torch.device("cuda:0")
+    torch.zeros(1, device=dev)  # creates the primary context
+    (err,) = cu.cuInit(0)
+    assert err == cu.CUresult.CUDA_SUCCESS, err
+
+    def load(name):
+        md = json.load(open(os.path.join(REF, name + ".json")))
+        data = open(os.path.join(REF, name + ".cubin"), "rb").read()
+        err, mod = cu.cuModuleLoadData(data)
+        assert err == cu.CUresult.CUDA_SUCCESS, (name, err)
+        err, fn = cu.cuModuleGetFunction(mod, md["name"].encode())
+        assert err == cu.CUresult.CUDA_SUCCESS, (name, err)
+        return mod, fn, md
+
+    def launch(k, grid, args):
+        _, fn, md = k
+        ptrs = (ctypes.c_void_p * len(args))(*[ctypes.addressof(a) for a in args])
+        st = torch.cuda.current_stream().cuda_stream
+        (err,) = cu.cuLaunchKernel(fn, grid, 1, 1, md["num_warps"] * 32, 1, 1, md["shared"], st,
+                                   ctypes.addressof(ptrs), 0)
+        assert err == cu.CUresult.CUDA_SUCCESS, err
+        torch.cuda.synchronize()
+
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    I = ctypes.c_int32  # noqa: E741
+    NULL = ctypes.c_void_p(0)
+    out = {"generator": "SplitMix64 counter stream, oracle.uniform (see oracle/ctb_oracle.c)",
+           "kernels": "reference TTIR / Python-Triton twins compiled by oracle/build_ref.py",
+           "vadd": [], "rowsum": [], "softmax": {}}
+    arrays = {}
+
+    k = load("vadd_ttir")
+    for n, sa, sb in VADD_CASES:
+        a = torch.from_numpy(O.uniform(n, sa)).to(dev)
+        b = torch.from_numpy(O.uniform(n, sb)).to(dev)
+        c = torch.zeros(n, device=dev)
+        launch(k, (n + 1023) // 1024, [P(a), I(n), I(1), P(b), I(n), I(1), P(c), I(n), I(1), NULL, NULL])
+        hc = c.cpu().numpy()
+        out["vadd"].append({"n": n, "seed_a": sa, "seed_b": sb, "sha256": sha(hc),
+                            "head": hc[:8].tolist()})
+        print("vadd", n, sha(hc)[:16])
+
+    k = load("rowsum_ttir")
+    gss, gsa = k[2]["global_scratch_size"], k[2]["global_scratch_align"]
+    for m, n, seed in ROWSUM_CASES:
+        a_jl = O.uniform(m * n, seed, lo=0.0, hi=1.0).reshape(n, m)  # Julia m x n, stride (1, m)
+        a = torch.from_numpy(a_jl).to(dev)
+        o = torch.zeros(m, device=dev)
+        grid = (m + 63) // 64
+        scratch = torch.zeros(grid * gss + gsa, dtype=torch.uint8, device=dev)
+        sp = ctypes.c_void_p((scratch.data_ptr() + gsa - 1) // gsa * gsa)
+        launch(k, grid, [P(a), I(m), I(n), I(1), I(m), P(o), I(m), I(1), I(1), I(m), sp, NULL])
+        ho = o.cpu().numpy()
+        out["rowsum"].append({"m": m, "n": n, "seed": seed, "lo": 0.0, "hi": 1.0, "sha256": sha(ho)})
+        arrays[f"rowsum_{m}x{n}"] = ho
+        print("rowsum", m, n, sha(ho)[:16])
+
+    k = load("softmax_py")
+    n_rows, n_cols, seed, grid = SOFTMAX_CASE
+    x_jl = O.uniform(n_rows * n_cols, seed, lo=0.0, hi=1.0).reshape(n_cols, n_rows)
+    x = torch.from_numpy(x_jl).to(dev)
+    y = torch.zeros_like(x)
+    launch(k, grid, [P(y), P(x), I(n_rows), I(n_cols), I(n_rows), I(n_rows), NULL, NULL])
+    hy = y.cpu().numpy()
+    out["softmax"] = {"n_rows": n_rows, "n_cols": n_cols, "seed": seed, "lo": 0.0, "hi": 1.0,
+                      "grid": grid, "sha256": sha(hy), "sampled_columns": SOFTMAX_COLS}
+    arrays["softmax_sampled"] = hy[SOFTMAX_COLS]
+    print("softmax", sha(hy)[:16])
+
+    dst = sys.argv[1] if len(sys.argv) > 1 else HERE
+    os.makedirs(dst, exist_ok=True)
+    with open(os.path.join(dst, "ref_goldens.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    np.savez_compressed(os.path.join(dst, "ref_goldens.npz"), **arrays)
+    print("written", os.path.join(dst, "ref_goldens.json"))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
