@@ -195,9 +195,10 @@ def time_device(case, steps, warmup, dist_on):
     return total, sum(per) / len(per)
 
 
-def time_e2e(case, steps, dev):
+def time_e2e(case, steps, dev, dist_on=False):
     """Through the public API with host buffers: per step a pinned host->device
-    copy of the inputs, the kernel, and a device->host copy of the result."""
+    copy of the inputs, the kernel, and a device->host copy of the result.
+    Returns (ms per step, max over ranks; H2D bytes; D2H bytes) per rank."""
     import torch
 
     hin = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in case.inputs]
@@ -215,6 +216,9 @@ def time_e2e(case, steps, dev):
 
     step()
     torch.cuda.synchronize()
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(st)
     for _ in range(steps):
@@ -222,6 +226,11 @@ def time_e2e(case, steps, dev):
     e.record(st)
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / steps
+    if dist_on:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
     return ms, case.bytes_in(), case.bytes_out()
 
 
@@ -455,9 +464,9 @@ def run_ours(args):
         res = {"value": round(value, 3), "unit": unit, "ms_per_step": round(total_ms / steps, 5),
                "roofline": roofline(name, mean_ms, peaks, peak_src, traffic),
                "gpu_launches": steps}
-        if want_e2e and rank == 0:
+        if want_e2e:
             k = max(2, min(steps, 10))
-            ms, bi, bo = time_e2e(case, k, dev)
+            ms, bi, bo = time_e2e(case, k, dev, dist_on)
             res["e2e"] = {"value": round(world * work / (ms * 1e-3) / scale, 3), "unit": unit,
                           "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
         case.free()
