@@ -390,6 +390,20 @@ def cpu_measure(name, budget_s):
 
 
 # ---------------------------------------------------------------------------- main
+class stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration of the block."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -440,7 +454,11 @@ def run_ours(args):
     if dist_on:
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # NCCL announces its version on stdout at communicator set-up; keep
+        # stdout for the single JSON line.
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            dist.barrier()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     import cutile_b200
