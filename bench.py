@@ -49,6 +49,8 @@ def _wl():
                    4 * 131072 * 512 + 4 * 131072),
         "layernorm": ("layernorm-fwd f32, 16384 rows x 4096, eps 1e-5", "GB/s", "hbm",
                       2 * 4 * 16384 * 4096 + 2 * 4 * 4096 + 2 * 4 * 16384),
+        "layernorm_bwd": ("layernorm-bwd f32, 16384 rows x 4096 (dx, dw, db)", "GB/s", "hbm",
+                          3 * 4 * 16384 * 4096 + 4 * 4 * 4096 + 2 * 4 * 16384),
         "gemm": ("f16 GEMM M=N=K=8192, f32 accumulate, f16 out", "TFLOP/s", "tensor",
                  2 * 8192 ** 3),
         "bgemm": ("f16 batched GEMM 32 x (2048 x 2048 x 2048)", "TFLOP/s", "tensor",
@@ -61,7 +63,7 @@ def _wl():
 
 
 WORKLOADS = _wl()
-SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "gemm", "bgemm", "fmha", "fmha_causal"]
+SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "gemm", "bgemm", "fmha", "fmha_causal"]
 
 
 def load_peaks():
@@ -127,6 +129,19 @@ class Case:
             rs = T.empty(16384, device=dev)
             self.run = lambda: ops.layernorm_fwd(x, w, b, 1e-5, y, mu, rs)
             self.inputs, self.outputs = [x, w, b], [y, mu, rs]
+        elif name == "layernorm_bwd":
+            x = ops.fill_normal(T.empty(16384, 4096, device=dev), seed)
+            dy = ops.fill_normal(T.empty(16384, 4096, device=dev), seed + 3)
+            w = ops.fill_normal(T.empty(4096, device=dev), seed + 1, 1.0, 0.1)
+            b = ops.fill_normal(T.empty(4096, device=dev), seed + 2, 0.0, 0.1)
+            _, mu, rs = ops.layernorm_fwd(x, w, b, 1e-5)
+            dx = T.empty_like(x)
+            dw = T.empty(4096, device=dev)
+            db = T.empty(4096, device=dev)
+            groups = ops.layernorm_bwd_groups(4096, 16384)
+            part = T.empty(2 * groups * 4096, device=dev)
+            self.run = lambda: ops.layernorm_bwd(x, dy, w, mu, rs, dx, dw, db, part, groups)
+            self.inputs, self.outputs = [x, dy, w, mu, rs], [dx, dw, db]
         elif name == "gemm":
             A = ops.fill_uniform(T.empty(8192, 8192, dtype=T.float16, device=dev), seed)
             B = ops.fill_uniform(T.empty(8192, 8192, dtype=T.float16, device=dev), seed + 1)
@@ -358,6 +373,16 @@ def cpu_measure(name, budget_s):
         v = loop(lambda: O.layernorm_f32_into(x, w, b, y, mu, rs, n, rows, 1e-5),
                  2 * 4 * rows * n) / 1e9
         return v, f"{rows} of 16384 rows x 4096, repeated for {budget_s:.0f} s", threads
+    if name == "layernorm_bwd":
+        rows, n = 1024, 4096
+        x = rng.standard_normal((rows, n)).astype(np.float32)
+        dy = rng.standard_normal((rows, n)).astype(np.float32)
+        w = np.ones(n, np.float32)
+        mu = x.mean(axis=1).astype(np.float32)
+        rs = (1 / np.sqrt(x.var(axis=1) + 1e-5)).astype(np.float32)
+        v = loop(lambda: O.layernorm_bwd(x, dy, w, mu, rs), 3 * 4 * rows * n) / 1e9
+        return v, (f"{rows} of 16384 rows x 4096 (oracle C/OpenMP port, double accumulation), "
+                   f"repeated for {budget_s:.0f} s"), threads
     if name in ("gemm", "bgemm"):
         s = 2048
         A = rng.uniform(-1, 1, (s, s)).astype(np.float32)

@@ -307,6 +307,34 @@ int L_layernorm(const ctb_array* x, const double* s, cudaStream_t st) {
                                X.strides[1], Y.strides[1], (float)s[0], st);
 }
 
+// layernorm_bwd(DX, DY, DW, DB, X, W, Mean, Rstd, PARTIAL): X/DY/DX Julia
+// (N x M) with contiguous columns; PARTIAL is Julia (N x 2G) workspace.
+int L_layernorm_bwd(const ctb_array* a, const double*, cudaStream_t st) {
+  const ctb_array &DX = a[0], &DY = a[1], &DW = a[2], &DB = a[3], &X = a[4], &W = a[5],
+                  &Mu = a[6], &Rs = a[7], &P = a[8];
+  for (int i = 0; i < 9; ++i)
+    if (a[i].dtype != CTB_F32) return set_error(CTB_ERR_DTYPE, "layernorm_bwd: Float32 only");
+  if (int rc = need_dims(X, 2, "layernorm_bwd", "X")) return rc;
+  const int n = X.sizes[0], rows = X.sizes[1];
+  if (DX.ndim != 2 || DY.ndim != 2 || DX.sizes[0] != n || DX.sizes[1] != rows ||
+      DY.sizes[0] != n || DY.sizes[1] != rows)
+    return set_error(CTB_ERR_SHAPE, "layernorm_bwd: X, DY, DX sizes differ");
+  if (W.sizes[0] != n || DW.sizes[0] != n || DB.sizes[0] != n || Mu.sizes[0] != rows ||
+      Rs.sizes[0] != rows)
+    return set_error(CTB_ERR_SHAPE, "layernorm_bwd: W/DW/DB need N, Mean/Rstd need M elements");
+  int64_t pe = 1;
+  for (int d = 0; d < P.ndim; ++d) pe *= P.sizes[d];
+  if (pe < 2 * (int64_t)n || pe % (2 * (int64_t)n) != 0)
+    return set_error(CTB_ERR_SHAPE, "layernorm_bwd: PARTIAL must hold 2 x groups x N floats");
+  if (X.strides[0] != 1 || DY.strides[0] != 1 || DX.strides[0] != 1)
+    return set_error(CTB_ERR_LAYOUT, "layernorm_bwd: dim 1 must be contiguous (stride 1)");
+  return ctb_layernorm_bwd_f32((const float*)X.ptr, (const float*)DY.ptr, (const float*)W.ptr,
+                               (const float*)Mu.ptr, (const float*)Rs.ptr, (float*)DX.ptr,
+                               (float*)DW.ptr, (float*)DB.ptr, n, rows, X.strides[1],
+                               DY.strides[1], DX.strides[1], (float*)P.ptr,
+                               (int32_t)(pe / (2 * (int64_t)n)), st);
+}
+
 // Column-major operand check for matmul: stride (1, ld).
 int colmajor_ld(const ctb_array& a, const char* which, int64_t* ld) {
   if (a.strides[0] != 1)
@@ -379,6 +407,7 @@ const Entry kRegistry[] = {
     {"softmax", 2, 0, 16, 0, L_softmax},
     {"layernorm_fwd", 6, 1, 8, 0, L_layernorm},
     {"layer_norm_fwd", 6, 1, 8, 0, L_layernorm},
+    {"layernorm_bwd", 9, 0, 16, 0, L_layernorm_bwd},
     {"matmul", 3, 0, 6, 0, L_matmul},
     {"matmul16", 3, 0, 6, 0, L_matmul},
     {"batchmatmul", 3, 0, 6, 0, L_bmm},

@@ -219,58 +219,6 @@ static int launch_rowsum(const float* a, float* out, int m, int n, int64_t si, i
 }
 
 // =============================================================================
-// Register-resident row staging shared by softmax and layernorm: a CTA of
-// THREADS threads holds one row of up to THREADS*NV*4 floats, NV float4 per
-// thread, element index (k*THREADS + t)*4 + e. Padding slots get `pad`.
-// =============================================================================
-template <int THREADS, int NV, bool VEC>
-__device__ __forceinline__ void load_row(const float* __restrict__ p, int len, float pad,
-                                         float (&v)[NV * 4]) {
-  const int t = threadIdx.x;
-  if (VEC) {
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int idx = (k * THREADS + t) * 4;
-      if (idx < len) {  // len % 4 == 0 on this path
-        float4 q = ld_stream_f4(p + idx);
-        v[4 * k + 0] = q.x;
-        v[4 * k + 1] = q.y;
-        v[4 * k + 2] = q.z;
-        v[4 * k + 3] = q.w;
-      } else {
-        v[4 * k + 0] = v[4 * k + 1] = v[4 * k + 2] = v[4 * k + 3] = pad;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int idx = (k * THREADS + t) * 4 + e;
-        v[4 * k + e] = idx < len ? p[idx] : pad;
-      }
-  }
-}
-
-template <int THREADS, int NV, bool VEC>
-__device__ __forceinline__ void store_row(float* __restrict__ p, int len,
-                                          const float (&v)[NV * 4]) {
-  const int t = threadIdx.x;
-#pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int idx0 = (k * THREADS + t) * 4;
-    if (VEC) {
-      if (idx0 < len)
-        st_stream_f4(p + idx0, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (idx0 + e < len) p[idx0 + e] = v[4 * k + e];
-    }
-  }
-}
-
-// =============================================================================
 // softmax over contiguous vectors (reference: test/runtests.jl:102-118,
 // bench/bench.jl:147-164): NegInf padding, max-subtracted exp, sum, divide.
 // =============================================================================

@@ -76,6 +76,9 @@ SIGNATURES = {
     "ctb_rowsum_f32": [_P, _P, _I32, _I32, _I64, _I64, _I64, _P],
     "ctb_softmax_f32": [_P, _P, _I32, _I32, _I64, _I64, _P],
     "ctb_layernorm_fwd_f32": [_P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _F, _P],
+    "ctb_layernorm_bwd_f32": [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I64, _P,
+                              _I32, _P],
+    "ctb_layernorm_bwd_groups": [_I32, _I32],
     "ctb_gemm_f16": [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _P],
     "ctb_bgemm_f16": [_P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64,
                       _P],

@@ -109,6 +109,30 @@ def layernorm_fwd(x, w, b, eps=1e-5, out=None, mean=None, rstd=None):
     return out, mean, rstd
 
 
+def layernorm_bwd_groups(n, rows):
+    g = _lib.load().ctb_layernorm_bwd_groups(n, rows)
+    if g < 1:
+        _lib.check(-8)
+    return g
+
+
+def layernorm_bwd(x, dy, w, mean, rstd, dx=None, dw=None, db=None, partial=None, groups=None):
+    """LayerNorm backward on row-major (rows, n) float32 tensors -> (dx, dw, db).
+    `partial` (2 * groups * n floats) is the workspace; allocated here when None."""
+    _need_cuda(x, dy, w, mean, rstd)
+    rows, n = x.shape
+    groups = layernorm_bwd_groups(n, rows) if groups is None else groups
+    dx = torch.empty_like(x) if dx is None else dx
+    dw = torch.empty(n, dtype=torch.float32, device=x.device) if dw is None else dw
+    db = torch.empty(n, dtype=torch.float32, device=x.device) if db is None else db
+    if partial is None:
+        partial = torch.empty(2 * groups * n, dtype=torch.float32, device=x.device)
+    _lib.call("ctb_layernorm_bwd_f32", x.data_ptr(), dy.data_ptr(), w.data_ptr(), mean.data_ptr(),
+              rstd.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), n, rows, x.stride(0),
+              dy.stride(0), dx.stride(0), partial.data_ptr(), groups, _st())
+    return dx, dw, db
+
+
 def matmul(A_t, B_t, C_t=None):
     """Julia C = A*B on column-major storage: A_t (K, M), B_t (N, K), C_t (N, M)."""
     _need_cuda(A_t, B_t)

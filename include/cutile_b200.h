@@ -98,8 +98,8 @@ int ctb_check_device(void* stream);
  * never depend on them). Replaces triton_kernel / compile_kernel
  * (reference: src/runtime.jl:128-160) and the candidate build of
  * get_kernel (src/shim.jl:20-36). Names: "vadd", "rowsum", "softmax",
- * "layernorm_fwd" (alias "layer_norm_fwd"), "matmul" (alias "matmul16"),
- * "batchmatmul", "fmha". */
+ * "layernorm_fwd" (alias "layer_norm_fwd"), "layernorm_bwd", "matmul" (alias
+ * "matmul16"), "batchmatmul", "fmha". */
 int ctb_find_kernel(const char* name, const int32_t* dtypes, int32_t ndtypes,
                     const int64_t* consts, int32_t nconsts, int32_t* handle);
 
@@ -148,6 +148,26 @@ int ctb_layernorm_fwd_f32(const float* x, const float* w, const float* b,
                           float* y, float* mean, float* rstd, int32_t n,
                           int32_t rows, int64_t ldx, int64_t ldy, float eps,
                           void* stream);
+
+/* LayerNorm backward over `rows` vectors of `n` contiguous elements (the
+ * cuTile example's backward kernels, layernorm.jl lines 118 and 186, not
+ * vendored in the reference): with xhat = (x - mean) * rstd, g = w * dy,
+ *   dx = (g - (xhat * mean(g * xhat) + mean(g))) * rstd,
+ *   dw = sum_rows dy * xhat,   db = sum_rows dy.
+ * `partial` is caller-provided workspace of 2 * groups * n floats (per-CTA dw
+ * and db partial rows, like the example's DW/DB group buffers; no locks are
+ * needed). groups >= 1; ctb_layernorm_bwd_groups() gives the value that fills
+ * the GPU. n <= 16384, n and the row strides multiples of 4, pointers
+ * 16-byte aligned. Deterministic for a given `groups`. */
+int ctb_layernorm_bwd_f32(const float* x, const float* dy, const float* w,
+                          const float* mean, const float* rstd, float* dx,
+                          float* dw, float* db, int32_t n, int32_t rows,
+                          int64_t ldx, int64_t lddy, int64_t lddx,
+                          float* partial, int32_t groups, void* stream);
+
+/* Recommended `groups` for ctb_layernorm_bwd_f32 on the current device
+ * (2 x SM count, at most rows); -1 if the device cannot be queried. */
+int ctb_layernorm_bwd_groups(int32_t n, int32_t rows);
 
 /* C = A * B, Float16 in, Float32 accumulate, Float16 out (round to nearest),
  * Julia column-major: A is M x K with column stride lda, B is K x N (ldb),

@@ -11,6 +11,9 @@
  *                                              test/runtests.jl:129-131, bench/bench.jl:188-189
  *   layernorm mean, biased var, rstd = 1/sqrt(var+eps), (x-mean)*rstd*w+b
  *             (cuTile example layernorm.jl:27 — not vendored: parity unpinned)
+ *   layernorm backward: dx = (g - (xhat*mean(g*xhat) + mean(g)))*rstd with
+ *             g = w*dy; dw = sum dy*xhat; db = sum dy (example layernorm.jl
+ *             lines 118/186 — not vendored: parity unpinned)
  * GEMM and attention are restated with numpy float64 in oracle/oracle.py.
  *
  * Checker variants accumulate in double. The *_f32 variants accumulate in
@@ -20,6 +23,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -189,5 +193,43 @@ void oracle_layernorm_fwd_f32(const float* x, const float* w, const float* b, fl
     for (int64_t i = 0; i < n; ++i) yr[i] = (xr[i] - mu) * rs * w[i] + b[i];
     mean[r] = mu;
     rstd[r] = rs;
+  }
+}
+
+/* ---- layernorm backward ------------------------------------------------------- */
+void oracle_layernorm_bwd(const float* x, const float* dy, const float* w, const float* mean,
+                          const float* rstd, float* dx, double* dw, double* db, int64_t n,
+                          int64_t rows) {
+  for (int64_t i = 0; i < n; ++i) dw[i] = db[i] = 0.0;
+#pragma omp parallel
+  {
+    double* ldw = (double*)calloc((size_t)n, sizeof(double));
+    double* ldb = (double*)calloc((size_t)n, sizeof(double));
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      const float* xr = x + r * n;
+      const float* gr = dy + r * n;
+      const double mu = mean[r], rs = rstd[r];
+      double s1 = 0.0, s2 = 0.0;
+      for (int64_t i = 0; i < n; ++i) {
+        const double xh = ((double)xr[i] - mu) * rs, g = (double)w[i] * gr[i];
+        s1 += g * xh;
+        s2 += g;
+        ldw[i] += (double)gr[i] * xh;
+        ldb[i] += gr[i];
+      }
+      const double c1 = s1 / (double)n, c2 = s2 / (double)n;
+      for (int64_t i = 0; i < n; ++i) {
+        const double xh = ((double)xr[i] - mu) * rs, g = (double)w[i] * gr[i];
+        dx[r * n + i] = (float)((g - (xh * c1 + c2)) * rs);
+      }
+    }
+#pragma omp critical
+    for (int64_t i = 0; i < n; ++i) {
+      dw[i] += ldw[i];
+      db[i] += ldb[i];
+    }
+    free(ldw);
+    free(ldb);
   }
 }

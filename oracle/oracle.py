@@ -14,7 +14,7 @@ layernorm with OpenMP; GEMM and attention are restated here in numpy float64
 * matmul:   ``Float32.(A) * Float32.(B)``; error = max|got-ref| / max|ref|
             bench/bench_f16.jl:27, 49-50; test/runtests.jl:95-98
 * isapprox: Julia ``≈`` = norm(x-y) <= rtol*max(norm(x), norm(y))
-* layernorm / batchmatmul / fmha: the cuTile examples are not vendored in the
+* layernorm fwd/bwd / batchmatmul / fmha: the cuTile examples are not vendored in the
   reference (parity unpinned); restated from their standard definitions.
 """
 import ctypes
@@ -64,6 +64,7 @@ def lib():
             "oracle_softmax_f32": [_P, _P, _I, _I, _I, _I],
             "oracle_layernorm_fwd": [_P] * 6 + [_I, _I, _I, _I, _D],
             "oracle_layernorm_fwd_f32": [_P] * 6 + [_I, _I, _I, _I, _D],
+            "oracle_layernorm_bwd": [_P] * 8 + [_I, _I],
             "oracle_set_threads": [ctypes.c_int],
         }
         for name, args in sig.items():
@@ -162,6 +163,22 @@ def layernorm_fwd(x, w, b, eps=1e-5):
     rs = np.empty(rows, np.float32)
     lib().oracle_layernorm_fwd(_p(x), _p(w), _p(b), _p(y), _p(mu), _p(rs), n, rows, n, n, eps)
     return y, mu, rs
+
+
+def layernorm_bwd(x, dy, w, mean, rstd):
+    """LayerNorm backward on (rows x n) float32 matrices -> (dx f32, dw f64, db f64)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    dy = np.ascontiguousarray(dy, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    mean = np.ascontiguousarray(mean, dtype=np.float32)
+    rstd = np.ascontiguousarray(rstd, dtype=np.float32)
+    rows, n = x.shape
+    dx = np.empty_like(x)
+    dw = np.empty(n, np.float64)
+    db = np.empty(n, np.float64)
+    lib().oracle_layernorm_bwd(_p(x), _p(dy), _p(w), _p(mean), _p(rstd), _p(dx), _p(dw), _p(db),
+                               n, rows)
+    return dx, dw, db
 
 
 def matmul(A, B):

@@ -41,7 +41,7 @@ def test_version_matches_header():
 
 
 @pytest.mark.parametrize("name,n", [("vadd", 3), ("rowsum", 2), ("softmax", 2),
-                                    ("layernorm_fwd", 6), ("layer_norm_fwd", 6), ("matmul", 3),
+                                    ("layernorm_fwd", 6), ("layer_norm_fwd", 6), ("layernorm_bwd", 9), ("matmul", 3),
                                     ("matmul16", 3), ("batchmatmul", 3), ("fmha", 4)])
 def test_registry_knows_the_seven_kernels(name, n):
     L = _lib.load()

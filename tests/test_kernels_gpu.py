@@ -147,6 +147,41 @@ def test_layernorm_fwd(dev, rows, n):
     assert O.isapprox(host(rs), rrs, 1e-5)
 
 
+@pytest.mark.parametrize("rows,n,groups", [(16384, 4096, None), (100, 4, None), (37, 1000, 5),
+                                           (64, 8192, None), (8, 12288, 3), (5, 16384, None),
+                                           (1000, 512, 1)])
+def test_layernorm_bwd(dev, rows, n, groups):
+    x = N((rows, n), 20, dev)
+    dy = N((rows, n), 21, dev)
+    w = N(n, 22, dev, mean=1.0, std=0.1)
+    b = N(n, 23, dev, std=0.1)
+    _, mu, rs = ops.layernorm_fwd(x, w, b, 1e-5)
+    dx, dw, db = ops.layernorm_bwd(x, dy, w, mu, rs, groups=groups)
+    rdx, rdw, rdb = O.layernorm_bwd(host(x), host(dy), host(w), host(mu), host(rs))
+    assert O.isapprox(host(dx), rdx, 1e-5)
+    assert O.isapprox(host(dw), rdw, 1e-5)
+    assert O.isapprox(host(db), rdb, 1e-5)
+
+
+def test_layernorm_bwd_registry(dev):
+    from cutile_b200 import TileArray
+
+    rows, n = 48, 1024
+    k = cb.triton_kernel("layernorm_bwd", [TileArray(torch.float32, 2)] * 2 +
+                         [TileArray(torch.float32, 1)] * 2 + [TileArray(torch.float32, 2)] +
+                         [TileArray(torch.float32, 1)] * 3 + [TileArray(torch.float32, 2)])
+    x, dy = N((rows, n), 24, dev), N((rows, n), 25, dev)
+    w = N(n, 26, dev, mean=1.0, std=0.1)
+    _, mu, rs = ops.layernorm_fwd(x, w, torch.zeros(n, device=dev))
+    dx = torch.empty_like(x)
+    dw, db = torch.empty(n, device=dev), torch.empty(n, device=dev)
+    partial = torch.empty(2 * 7, n, device=dev)  # Julia (N, 2G), G = 7
+    cb.launch(k, 1, dx, dy, dw, db, x, w, mu, rs, partial)
+    rdx, rdw, rdb = O.layernorm_bwd(host(x), host(dy), host(w), host(mu), host(rs))
+    assert O.isapprox(host(dx), rdx, 1e-5) and O.isapprox(host(dw), rdw, 1e-5)
+    assert O.isapprox(host(db), rdb, 1e-5)
+
+
 # ----------------------------------------------------------------------------- GEMM
 def gemm_case(dev, M, N_, K, seed, lda=None, ldb=None):
     lda = lda or M

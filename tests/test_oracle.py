@@ -93,3 +93,23 @@ def test_isapprox_semantics():
     assert O.isapprox([1.0, 2.0], [1.0, 2.0 + 1e-7], 1e-6)
     assert not O.isapprox([1.0, 2.0], [1.0, 2.1], 1e-6)
     assert not O.isapprox([np.nan], [np.nan], 1e-6)
+
+
+def test_layernorm_bwd_matches_autograd():
+    import torch
+
+    rows, n = 33, 256
+    x = O.normal(rows * n, 1).reshape(rows, n)
+    dy = O.normal(rows * n, 2).reshape(rows, n)
+    w = 1 + 0.1 * O.normal(n, 3)
+    b = 0.1 * O.normal(n, 4)
+    _, mu, rs = O.layernorm_fwd(x, w, b, 1e-5)
+    dx, dw, db = O.layernorm_bwd(x, dy, w, mu, rs)
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    wt = torch.tensor(w, dtype=torch.float64, requires_grad=True)
+    bt = torch.tensor(b, dtype=torch.float64, requires_grad=True)
+    torch.nn.functional.layer_norm(xt, (n,), wt, bt, eps=1e-5).backward(
+        torch.tensor(dy, dtype=torch.float64))
+    assert O.isapprox(dx, xt.grad.numpy(), 1e-6)
+    assert O.isapprox(dw, wt.grad.numpy(), 1e-6)
+    assert O.isapprox(db, bt.grad.numpy(), 1e-6)
