@@ -15,6 +15,7 @@
 #include "ctb_common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace ctb {
 
@@ -158,5 +159,73 @@ extern "C" int ctb_layernorm_bwd_f32(const float* x, const float* dy, const floa
   DeviceProps p;
   if (int rc = current_props(&p)) return rc;
   return launch_layernorm_bwd(x, dy, w, mean, rstd, dx, dw, db, n, rows, ldx, lddy, lddx, partial,
+                              groups, static_cast<cudaStream_t>(stream));
+}
+
+// =============================================================================
+// Allocation-free LayerNorm backward.
+//
+// Some callers cannot allocate device memory at the point where they need a
+// backward pass: a process that reserved its whole device-memory budget up
+// front for its own pool, or Julia code running where CUDA.jl's allocator
+// (which may trigger a garbage collection) must not be entered. For them this
+// entry point takes the dW/dB partial workspace from a fixed array compiled
+// into the library instead of from the caller.
+//
+// The array below is LNBWD_NOALLOC_FLOATS floats (4 MiB) and lives on every
+// GPU that loads the library until the process exits. In host code its name
+// is only a host-side stand-in, so its device address is fetched per device
+// with cudaGetSymbolAddress on the first call made on that device (with that
+// device current); make that first call before any stream capture. All calls
+// share the one array: two calls whose kernels overlap on a GPU (different
+// streams, or different host threads on one device) race and corrupt each
+// other's dW/dB. Each call writes every partial row it later reads, so no
+// clearing is needed between calls.
+// =============================================================================
+namespace ctb {
+
+constexpr int64_t LNBWD_NOALLOC_FLOATS = 1 << 20;  // 4 MiB
+static __device__ __align__(256) float g_lnbwd_noalloc_scratch[LNBWD_NOALLOC_FLOATS];
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64];
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  CTB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(CTB_ERR_NO_DEVICE, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_lnbwd_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(layernorm_bwd scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return CTB_OK;
+}
+
+}  // namespace ctb
+
+extern "C" int ctb_layernorm_bwd_f32_noalloc(const float* x, const float* dy, const float* w,
+                                             const float* mean, const float* rstd, float* dx,
+                                             float* dw, float* db, int32_t n, int32_t rows,
+                                             int64_t ldx, int64_t lddy, int64_t lddx,
+                                             int32_t groups, void* stream) {
+  clear_error();
+  DeviceProps p;
+  if (int rc = current_props(&p)) return rc;
+  if (n <= 0 || rows < 0) return set_error(CTB_ERR_SHAPE, "layernorm_bwd_noalloc: bad sizes");
+  if (2 * (int64_t)n > LNBWD_NOALLOC_FLOATS)
+    return set_error(CTB_ERR_SHAPE, "layernorm_bwd_noalloc: n too large for the built-in scratch");
+  const int64_t cap = LNBWD_NOALLOC_FLOATS / (2 * (int64_t)n);  // partial rows that fit
+  if (groups <= 0) groups = (int32_t)std::min<int64_t>(layernorm_bwd_groups(n, rows, p.sm_count), cap);
+  if ((int64_t)std::min(groups, std::max(rows, 1)) * 2 * n > LNBWD_NOALLOC_FLOATS)
+    return set_error(CTB_ERR_SHAPE,
+                     "layernorm_bwd_noalloc: 2 x groups x n exceeds the built-in scratch of " +
+                         std::to_string(LNBWD_NOALLOC_FLOATS) + " floats");
+  float* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  return launch_layernorm_bwd(x, dy, w, mean, rstd, dx, dw, db, n, rows, ldx, lddy, lddx, scratch,
                               groups, static_cast<cudaStream_t>(stream));
 }

@@ -169,6 +169,24 @@ int ctb_layernorm_bwd_f32(const float* x, const float* dy, const float* w,
  * (2 x SM count, at most rows); -1 if the device cannot be queried. */
 int ctb_layernorm_bwd_groups(int32_t n, int32_t rows);
 
+/* Allocation-free variant of ctb_layernorm_bwd_f32 (no counterpart in the
+ * reference). For callers that cannot allocate device memory when they need
+ * the backward pass — a process that reserved its whole device-memory budget
+ * for its own pool, or Julia code running where CUDA.jl's allocator must not
+ * be entered. The dW/dB partial workspace comes from a 4 MiB array built
+ * into the library (held on every GPU that loads it until exit) instead of
+ * from the caller; the caller still passes every input and output.
+ * groups <= 0 picks the largest useful value that fits; 2 * groups * n must
+ * not exceed 1,048,576 floats (CTB_ERR_SHAPE otherwise). The first call on a
+ * device looks up the array's device address; make it before any stream
+ * capture. All calls share the array: calls that overlap on a GPU race. */
+int ctb_layernorm_bwd_f32_noalloc(const float* x, const float* dy,
+                                  const float* w, const float* mean,
+                                  const float* rstd, float* dx, float* dw,
+                                  float* db, int32_t n, int32_t rows,
+                                  int64_t ldx, int64_t lddy, int64_t lddx,
+                                  int32_t groups, void* stream);
+
 /* C = A * B, Float16 in, Float32 accumulate, Float16 out (round to nearest),
  * Julia column-major: A is M x K with column stride lda, B is K x N (ldb),
  * C is M x N (ldc). cuTile `matmul16(A, B, C, tm, tn, tk)` (reference:
