@@ -8,15 +8,16 @@
 // One CTA = one (batch*head, 256-query block), split into two 128-row query
 // tiles Q0/Q1 that ping-pong: while softmax warpgroup 0 turns S0 into P0,
 // the tensor core computes S1 (or P1*V), and vice versa.
-//   warps 0-7   softmax + epilogue for Q0: a score row is split between two
-//               threads (64 columns each), warp w reads TMEM lanes 32*(w%4)
-//   warps 8-15  softmax + epilogue for Q1
-//   warp  16    TMEM owner + MMA issuer (one thread)
-//   warp  17    TMA producer (one thread): Q once, then a 2-stage K / V ring
+//   warps 0-3   softmax + epilogue for Q0, one thread per query row holding
+//               its 128 scores in registers (warp w reads TMEM lanes 32*(w%4))
+//   warps 4-7   softmax + epilogue for Q1
+//   warp  8     TMEM owner + MMA issuer (one thread)
+//   warp  9     TMA producer (one thread): Q once, then a 2-stage K / V ring
+//   warps 10-15 idle; with warps 8-9 they lend registers (setmaxnreg) so the
+//               softmax warps can run at 192 registers
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
-// P_t (Float16, two per 32-bit column) overwrites S_t columns 0-31 (keys
-// 0-63) and 64-95 (keys 64-127) once those scores have been read, and feeds
-// P_t*V as the TMEM A operand.
+// P_t (Float16, two per 32-bit column) overwrites S_t columns 0-63 once the
+// row's scores are in registers, and feeds P_t*V as the TMEM A operand.
 // Scores are kept in log2 units (exp2 with scale*log2(e) folded in). The
 // running max is only moved when it grows by more than 8 (a factor 256), so
 // the O rescale in TMEM is rare; numerator and denominator always share the
@@ -37,13 +38,16 @@ namespace fmha {
 constexpr int D = 128;            // head dim handled by this kernel
 constexpr int BQ = 128;           // rows per query tile (UMMA M)
 constexpr int BKV = 128;          // keys per block (UMMA N of S, K of P*V)
-constexpr int SM_THREADS_PER_TILE = 256;      // 8 softmax warps per query tile
-constexpr int MMA_WARP = 16, TMA_WARP = 17;
-constexpr int THREADS = 18 * 32;
+constexpr int SM_THREADS_PER_TILE = 128;      // 4 softmax warps per query tile
+constexpr int MMA_WARP = 8, TMA_WARP = 9;     // warps 10-15 only lend registers
+constexpr int THREADS = 16 * 32;
+// Register split (setmaxnreg): launched at 128 per thread (512 x 128 = 65536);
+// the two softmax warpgroups rise to 192, the other two drop to 64:
+// 256 x 192 + 256 x 64 = 65536.
+constexpr int REG_SOFTMAX = 192, REG_OTHER = 64;
 constexpr int TILE_BYTES = BQ * D * 2;       // 32 KB: one 128 x 128 f16 tile
 constexpr int HALF_BYTES = TILE_BYTES / 2;   // one 64-wide (128-byte) TMA box
-constexpr int XCHG_BYTES = 2 * 2 * BQ * 4;    // per-row partial max / sum exchange
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + XCHG_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 constexpr unsigned ERR_BIT = 2u;
 
@@ -141,8 +145,8 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
   mma_commit(s_full_t);
 }
 
-// O_t (+)= P_t V for one key block: P_t from TMEM (keys 0-63 packed in S_t
-// columns 0-31, keys 64-127 in columns 64-95; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
+// O_t (+)= P_t V for one key block: P_t from TMEM (128 keys packed in S_t
+// columns 0-63; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
 // 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
 __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j) {
   using namespace sm100;
@@ -150,7 +154,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
   const uint32_t va = sVa + stage * TILE_BYTES;
 #pragma unroll
   for (int kk = 0; kk < BKV / 16; ++kk)
-    mma_f16_ts(tmem + 256 + t * D, tmem + t * BKV + (kk >> 2) * 64 + (kk & 3) * 8,
+    mma_f16_ts(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
                smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
                (j > 0 || kk > 0) ? 1u : 0u);
 }
@@ -166,8 +170,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sQ = smem;                        // Q0, Q1
   uint8_t* sK = smem + 2 * TILE_BYTES;       // 2 stages
   uint8_t* sV = smem + 4 * TILE_BYTES;       // 2 stages
-  float* xchg = reinterpret_cast<float*>(smem + 6 * TILE_BYTES);  // [2 tiles][2 halves][128 rows]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES + XCHG_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -211,6 +214,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 8) {
+    // Control warpgroups (MMA issuer, TMA producer, idle warps): give
+    // registers to the softmax warps.
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_OTHER));
+  }
   if (warp == TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -271,56 +279,46 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(&o_full[0]);
       mma_commit(&o_full[1]);
     }
-  } else {
-    // ------------------------------------------------------------ softmax warps
-    // Tile t has 8 warps; a score row is split between two threads (one per
-    // 64-column half) that exchange their partial max through shared memory.
-    const int t = warp / 8;
-    const int ww = warp % 8;
-    const int quarter = ww & 3;  // TMEM lanes 32*quarter .. +31 (warp id mod 4)
-    const int half = ww >> 2;    // score / output columns 64*half .. +63
-    const int row = quarter * 32 + lane;
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax warpgroups
+    // One thread per query row, all 128 scores of a block in registers.
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFTMAX));
+    const int t = warp >> 2;        // query tile
+    const int quarter = warp & 3;   // TMEM lanes 32*quarter .. +31
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_col = tmem + lane_off + t * BKV + half * 64;
-    // P of this half goes into the first 32 of its own 64 S columns.
-    const uint32_t p_col = s_col;
-    const uint32_t o_col = tmem + lane_off + 256 + t * D + half * 64;
-    float* my_x = xchg + (t * 2 + half) * BQ;
-    const float* other_x = xchg + (t * 2 + (half ^ 1)) * BQ;
-    const int qrow = q0 + t * BQ + row;
+    const uint32_t s_col = tmem + lane_off + t * BKV;
+    const uint32_t o_col = tmem + lane_off + 256 + t * D;
+    const int qrow = q0 + t * BQ + quarter * 32 + lane;
     const float sl2 = p.scale_log2;
     float m_use = -INFINITY, l = 0.f;
     for (int j = 0; j < nb; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag, ERR_BIT)) break;
       tc_fence_after();
-      // Pass 1: this half's 64 scores -> partial row max, 32 columns at a time.
-      const int k0 = j * BKV + half * 64;
-      const bool need_mask =
-          (j * BKV + BKV > p.Sk) || (p.causal && j * BKV + BKV - 1 > q0 + t * BQ);
-      float mxa = -INFINITY, mxb = -INFINITY;
+      uint32_t r[4][32];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_col + h * 32, r);
-        tmem_ld_wait();
-        if (need_mask) {
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_col + c * 32, r[c]);
+      const int k0 = j * BKV;
+      const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > q0 + t * BQ);
+      tmem_ld_wait();
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int key = k0 + h * 32 + i;
-            if (key >= p.Sk || (p.causal && key > qrow)) r[i] = __float_as_uint(-INFINITY);
+            const int key = k0 + c * 32 + i;
+            if (key >= p.Sk || (p.causal && key > qrow)) r[c][i] = __float_as_uint(-INFINITY);
           }
-        }
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          mxa = max3(mxa, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          mxb = max3(mxb, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-        }
       }
-      my_x[row] = fmaxf(mxa, mxb);
-      // Both threads of a row meet here to combine their partial maxima.
-      named_barrier_sync(1 + t, SM_THREADS_PER_TILE);
-      const float mx = fmaxf(my_x[row], other_x[row]);
-      const float m_blk = mx * sl2;
+      float mx[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        mx[c] = __uint_as_float(r[c][0]);
+#pragma unroll
+        for (int i = 1; i < 31; i += 2)
+          mx[c] = max3(mx[c], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+        mx[c] = fmaxf(mx[c], __uint_as_float(r[c][31]));
+      }
+      const float m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
       float factor = 1.f;
       bool rescale = false;
       if (j == 0) {
@@ -331,41 +329,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_use = m_blk;
         rescale = true;
       }
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_t is stable here: P_t*V of block j-1 completed before S_t of block j.
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(o_col + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          tmem_st_32x32b_x32(o_col + c * 32, o);
-        }
-      }
       // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
       // (-inf) - (-inf) would be NaN, so shift by 0 for them.
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
       const uint64_t sl2x2 = f2_pack(sl2, sl2), nm2 = f2_pack(-mref, -mref);
       uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
-      // Pass 2 re-reads the scores 32 columns at a time (keeps registers low);
-      // chunk h's 16 packed P columns land in columns this thread already read.
+      // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read above.
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t rr[32], pk[16];
-        tmem_ld_32x32b_x32(s_col + h * 32, rr);
-        tmem_ld_wait();
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = k0 + h * 32 + i;
-            if (key >= p.Sk || (p.causal && key > qrow)) rr[i] = __float_as_uint(-INFINITY);
-          }
-        }
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const uint64_t x = f2_fma(f2_pack(__uint_as_float(rr[2 * i]),
-                                            __uint_as_float(rr[2 * i + 1])),
+          const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[c][2 * i]),
+                                            __uint_as_float(r[c][2 * i + 1])),
                                     sl2x2, nm2);
           float xa, xb;
           f2_unpack(x, xa, xb);
@@ -380,27 +356,36 @@ __global__ void __launch_bounds__(THREADS, 1)
           f2_unpack(e, ea, eb);
           pk[i] = pack_half2(ea, eb);
         }
-        tmem_st_32x32b_x16(p_col + h * 16, pk);
+        tmem_st_32x32b_x16(s_col + c * 16, pk);
       }
       float s0, s1, s2, s3;
       f2_unpack(acc0, s0, s1);
       f2_unpack(acc1, s2, s3);
       l += (s0 + s1) + (s2 + s3);
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_t is stable here: P_t*V of block j-1 completed before S_t of block j,
+        // and P_t*V of block j waits for this thread's p_full arrival below.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_col + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st_32x32b_x32(o_col + c * 32, o);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
     // ------------------------------------------------------------ epilogue
-    // Row sum = both halves' partial sums.
-    my_x[row] = l;
-    named_barrier_sync(1 + t, SM_THREADS_PER_TILE);
-    const float l_row = l + other_x[row];
     if (mbar_wait_bounded(&o_full[t], 0, abort_flag, ERR_BIT)) {
       tc_fence_after();
-      const float inv = 1.f / l_row;
-      __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D + half * 64;
+      const float inv = 1.f / l;
+      __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(o_col + c * 32, o);
         tmem_ld_wait();
