@@ -51,6 +51,8 @@ def _wl():
                       2 * 4 * 16384 * 4096 + 2 * 4 * 4096 + 2 * 4 * 16384),
         "layernorm_bwd": ("layernorm-bwd f32, 16384 rows x 4096 (dx, dw, db)", "GB/s", "hbm",
                           3 * 4 * 16384 * 4096 + 4 * 4 * 4096 + 2 * 4 * 16384),
+        "transpose": ("transpose f32 8192 x 8192 (extra: not a BASELINE config)", "GB/s", "hbm",
+                      2 * 4 * 8192 * 8192),
         "gemm": ("f16 GEMM M=N=K=8192, f32 accumulate, f16 out", "TFLOP/s", "tensor",
                  2 * 8192 ** 3),
         "bgemm": ("f16 batched GEMM 32 x (2048 x 2048 x 2048)", "TFLOP/s", "tensor",
@@ -63,7 +65,7 @@ def _wl():
 
 
 WORKLOADS = _wl()
-SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "gemm", "bgemm", "fmha", "fmha_causal"]
+SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "transpose", "gemm", "bgemm", "fmha", "fmha_causal"]
 
 
 def load_peaks():
@@ -142,6 +144,11 @@ class Case:
             part = T.empty(2 * groups * 4096, device=dev)
             self.run = lambda: ops.layernorm_bwd(x, dy, w, mu, rs, dx, dw, db, part, groups)
             self.inputs, self.outputs = [x, dy, w, mu, rs], [dx, dw, db]
+        elif name == "transpose":
+            x = ops.fill_uniform(T.empty(8192, 8192, device=dev), seed)
+            y = T.empty_like(x)
+            self.run = lambda: ops.transpose(x, y)
+            self.inputs, self.outputs = [x], [y]
         elif name == "gemm":
             A = ops.fill_uniform(T.empty(8192, 8192, dtype=T.float16, device=dev), seed)
             B = ops.fill_uniform(T.empty(8192, 8192, dtype=T.float16, device=dev), seed + 1)
@@ -373,6 +380,12 @@ def cpu_measure(name, budget_s):
         v = loop(lambda: O.layernorm_f32_into(x, w, b, y, mu, rs, n, rows, 1e-5),
                  2 * 4 * rows * n) / 1e9
         return v, f"{rows} of 16384 rows x 4096, repeated for {budget_s:.0f} s", threads
+    if name == "transpose":
+        x = rng.uniform(-1, 1, (8192, 2048)).astype(np.float32)
+        y = np.empty((2048, 8192), np.float32)
+        v = loop(lambda: np.copyto(y, x.T), 2 * 4 * x.size) / 1e9
+        return v, (f"8192 x 2048 of 8192 x 8192 with numpy copyto(x.T) (1 thread), "
+                   f"repeated for {budget_s:.0f} s"), 1
     if name == "layernorm_bwd":
         rows, n = 1024, 4096
         x = rng.standard_normal((rows, n)).astype(np.float32)

@@ -335,6 +335,19 @@ int L_layernorm_bwd(const ctb_array* a, const double*, cudaStream_t st) {
                                (int32_t)(pe / (2 * (int64_t)n)), st);
 }
 
+// transpose(x, y): y = x', both Julia 2-D with contiguous columns.
+int L_transpose(const ctb_array* a, const double*, cudaStream_t st) {
+  const ctb_array &X = a[0], &Y = a[1];
+  if (int rc = need_dims(X, 2, "transpose", "x")) return rc;
+  if (int rc = need_dims(Y, 2, "transpose", "y")) return rc;
+  if (X.dtype != Y.dtype) return set_error(CTB_ERR_DTYPE, "transpose: x and y element types differ");
+  if (Y.sizes[0] != X.sizes[1] || Y.sizes[1] != X.sizes[0])
+    return set_error(CTB_ERR_SHAPE, "transpose: y must be size(x, 2) x size(x, 1)");
+  if (X.strides[0] != 1 || Y.strides[0] != 1)
+    return set_error(CTB_ERR_LAYOUT, "transpose: dim 1 must be contiguous (stride 1)");
+  return ctb_transpose(X.dtype, X.ptr, Y.ptr, X.sizes[0], X.sizes[1], X.strides[1], Y.strides[1], st);
+}
+
 // Column-major operand check for matmul: stride (1, ld).
 int colmajor_ld(const ctb_array& a, const char* which, int64_t* ld) {
   if (a.strides[0] != 1)
@@ -413,6 +426,7 @@ const Entry kRegistry[] = {
     {"batchmatmul", 3, 0, 6, 0, L_bmm},
     {"batch_matmul", 3, 0, 6, 0, L_bmm},
     {"fmha", 4, 2, 16, 0, L_fmha},
+    {"transpose", 2, 0, 8, 0, L_transpose},
 };
 constexpr int kRegistrySize = sizeof(kRegistry) / sizeof(kRegistry[0]);
 

@@ -81,6 +81,7 @@ SIGNATURES = {
     "ctb_layernorm_bwd_groups": [_I32, _I32],
     "ctb_layernorm_bwd_f32_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64,
                                       _I64, _I32, _P],
+    "ctb_transpose": [_I32, _P, _P, _I32, _I32, _I64, _I64, _P],
     "ctb_gemm_f16": [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _P],
     "ctb_bgemm_f16": [_P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64,
                       _P],

@@ -133,6 +133,19 @@ def layernorm_bwd(x, dy, w, mean, rstd, dx=None, dw=None, db=None, partial=None,
     return dx, dw, db
 
 
+def transpose(x, out=None):
+    """Julia y = x' on column-major storage: x_t (N, M) holds the Julia M x N
+    matrix; returns y_t (M, N) holding the Julia N x M transpose."""
+    _need_cuda(x)
+    N, M = x.shape
+    if x.stride(1) != 1:
+        raise _lib.B200Error(-4, "transpose: columns must be contiguous")
+    out = torch.empty(M, N, dtype=x.dtype, device=x.device) if out is None else out
+    _lib.call("ctb_transpose", _DT[x.dtype], x.data_ptr(), out.data_ptr(), M, N, x.stride(0),
+              out.stride(0), _st())
+    return out
+
+
 def matmul(A_t, B_t, C_t=None):
     """Julia C = A*B on column-major storage: A_t (K, M), B_t (N, K), C_t (N, M)."""
     _need_cuda(A_t, B_t)

@@ -99,7 +99,7 @@ int ctb_check_device(void* stream);
  * (reference: src/runtime.jl:128-160) and the candidate build of
  * get_kernel (src/shim.jl:20-36). Names: "vadd", "rowsum", "softmax",
  * "layernorm_fwd" (alias "layer_norm_fwd"), "layernorm_bwd", "matmul" (alias
- * "matmul16"), "batchmatmul", "fmha". */
+ * "matmul16"), "batchmatmul", "fmha", "transpose". */
 int ctb_find_kernel(const char* name, const int32_t* dtypes, int32_t ndtypes,
                     const int64_t* consts, int32_t nconsts, int32_t* handle);
 
@@ -186,6 +186,12 @@ int ctb_layernorm_bwd_f32_noalloc(const float* x, const float* dy,
                                   float* db, int32_t n, int32_t rows,
                                   int64_t ldx, int64_t lddy, int64_t lddx,
                                   int32_t groups, void* stream);
+
+/* y = x^T: x is Julia M x N (column stride ldx), y is N x M (column stride
+ * ldy); dtype F16/F32/F64; a copy, bit-exact. cuTile example transpose.jl
+ * (not vendored in the reference; research/bench_final.log:10). */
+int ctb_transpose(int32_t dtype, const void* x, void* y, int32_t M, int32_t N,
+                  int64_t ldx, int64_t ldy, void* stream);
 
 /* C = A * B, Float16 in, Float32 accumulate, Float16 out (round to nearest),
  * Julia column-major: A is M x K with column stride lda, B is K x N (ldb),

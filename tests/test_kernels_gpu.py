@@ -182,6 +182,25 @@ def test_layernorm_bwd_registry(dev):
     assert O.isapprox(host(db), rdb, 1e-5)
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.float64])
+@pytest.mark.parametrize("M,N_", [(8192, 8192), (1000, 37), (1, 5), (65, 129)])
+def test_transpose_bit_exact(dev, dt, M, N_):
+    x = U((N_, M), 90, dev, dt)  # Julia M x N
+    y = ops.transpose(x)         # Julia N x M
+    assert host(y).tobytes() == np.ascontiguousarray(host(x).T).tobytes()
+
+
+def test_transpose_registry_padded_columns(dev):
+    from cutile_b200 import TileArray
+
+    k = cb.triton_kernel("transpose", [TileArray(torch.float32, 2)] * 2)
+    store = U((50, 80), 91, dev)
+    x = cb.JlArray(store[:, :70], (70, 50), (1, 80))  # Julia 70 x 50, column stride 80
+    y = torch.zeros(70, 50, device=dev)               # Julia 50 x 70
+    cb.launch(k, 1, x, y)
+    assert host(y).tobytes() == np.ascontiguousarray(host(store)[:, :70].T).tobytes()
+
+
 # ----------------------------------------------------------------------------- GEMM
 def gemm_case(dev, M, N_, K, seed, lda=None, ldb=None):
     lda = lda or M
