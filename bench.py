@@ -314,6 +314,42 @@ class ClockSampler:
                 "samples": len(self.rows), "samples_under_load": len(load)}
 
 
+def launch_path(dev):
+    """Per-launch cost of a tiny softmax (64 x 1024) through the Python C-ABI
+    binding: eager (host flattening + ctypes + launch) vs the same 100
+    launches captured once in a CUDA graph and replayed."""
+    import torch
+    from cutile_b200 import ops
+
+    x = ops.fill_normal(torch.empty(64, 1024, device=dev), 5)
+    y = torch.empty_like(x)
+    for _ in range(10):
+        ops.softmax(x, y)
+    torch.cuda.synchronize()
+    n = 2000
+    t0 = time.perf_counter()
+    for _ in range(n):
+        ops.softmax(x, y)
+    torch.cuda.synchronize()
+    eager_us = (time.perf_counter() - t0) / n * 1e6
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(100):
+            ops.softmax(x, y)
+    g.replay()
+    torch.cuda.synchronize()
+    reps = 20
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        g.replay()
+    torch.cuda.synchronize()
+    graph_us = (time.perf_counter() - t0) / (reps * 100) * 1e6
+    return {"workload": "softmax 64 x 1024 f32, back-to-back launches, host wall clock",
+            "eager_us_per_launch": round(eager_us, 2), "graph_us_per_launch": round(graph_us, 2)}
+
+
 def roofline(name, mean_ms, peaks, peak_src, traffic):
     _, unit, bound, work = WORKLOADS[name]
     if bound == "hbm":
@@ -546,6 +582,7 @@ def run_ours(args):
             suite[name] = measure(name, steps, max(3, args.warmup), True,
                                   True, args.cpu_budget / 3)
             suite[name]["config"] = WORKLOADS[name][0]
+    lp = launch_path(dev) if (args.suite and rank == 0) else None
     if rank == 0:
         sampler.stop()
     if rank == 0:
@@ -560,7 +597,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (126 MB): 268 MB read + 268 MB written per step"},
             "roofline": h["roofline"], "cpu_baseline": h.get("cpu_baseline"),
             "e2e": h.get("e2e"), "gpu_launches": h["gpu_launches"], "clocks": clocks,
-            "library": cutile_b200.library_path(), "suite": suite,
+            "library": cutile_b200.library_path(), "suite": suite, "launch_path": lp,
         }
         print(json.dumps(line), flush=True)
     if dist_on:
