@@ -119,6 +119,21 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
   return f2_pack(ra, rb);
 }
 
+#ifdef CTB_FMHA_TRACE
+// Debug-only timeline of CTA 0 (clock64 cycles): [event][block] where events
+// are 0/1 softmax tile t got S (t = 0, 1), 2/3 softmax tile t arrived P,
+// 4/5 MMA issued P_t*V, 6/7 MMA issued S_t(j+1), 8 MMA got V.
+__device__ long long g_fmha_trace[9][128];
+#define FMHA_TRACE(ev, j)                                                      \
+  do {                                                                       \
+    if (blockIdx.x == 0 && (j) < 128) g_fmha_trace[(ev)][(j)] = clock64();   \
+  } while (0)
+#else
+#define FMHA_TRACE(ev, j) \
+  do {                    \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -259,20 +274,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t ph = (j >> 1) & 1, phn = ((j + 1) >> 1) & 1;
         const bool more = j + 1 < nb;
         if (!(ok = mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT))) break;
+        FMHA_TRACE(8, j);
         if (!(ok = mbar_wait_bounded(&p_full[0], j & 1, abort_flag, ERR_BIT))) break;
         tc_fence_after();
         issue_pv(tmem, sVa, 0, s, j);
+        FMHA_TRACE(4, j);
         if (more) {
           if (!(ok = mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT))) break;
           tc_fence_after();
           issue_s(tmem, sQa, sKa, 0, sn, &s_full[0]);
+          FMHA_TRACE(6, j);
         }
         if (!(ok = mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT))) break;
         tc_fence_after();
         issue_pv(tmem, sVa, 1, s, j);
+        FMHA_TRACE(5, j);
         mma_commit(&v_empty[s]);
         if (more) {
           issue_s(tmem, sQa, sKa, 1, sn, &s_full[1]);
+          FMHA_TRACE(7, j);
           mma_commit(&k_empty[sn]);
         }
       }
@@ -293,6 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m_use = -INFINITY, l = 0.f;
     for (int j = 0; j < nb; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag, ERR_BIT)) break;
+      if (threadIdx.x % 128 == 0) FMHA_TRACE(t, j);
       tc_fence_after();
       uint32_t r[4][32];
 #pragma unroll
@@ -378,6 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
+      if (threadIdx.x % 128 == 0) FMHA_TRACE(2 + t, j);
     }
     // ------------------------------------------------------------ epilogue
     if (mbar_wait_bounded(&o_full[t], 0, abort_flag, ERR_BIT)) {
@@ -416,6 +438,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace fmha
 
 int fmha_take_device_error(unsigned int* out) { return take_device_error(out); }
+
+#ifdef CTB_FMHA_TRACE
+extern "C" int ctb_fmha_trace_read(long long* out) {
+  return cudaMemcpyFromSymbol(out, fmha::g_fmha_trace, sizeof(fmha::g_fmha_trace)) == cudaSuccess ? 0 : -6;
+}
+#endif
 
 static bool g_fmha_attr_done[64];
 static std::mutex g_fmha_mu;
