@@ -304,6 +304,29 @@ def test_fmha(dev, B, H, S, D, causal):
     fmha_case(dev, B, H, S, D, causal, 50)
 
 
+@pytest.mark.parametrize("causal", [False, True])
+def test_fmha_running_max_grows(dev, causal):
+    """Scores that grow along the key axis force the running max up by more
+    than the rescale threshold many times (the O rescale and exponential-redo
+    paths), and large negative early scores exercise exp2 underflow."""
+    B, H, S, D = 1, 2, 1024, 128
+    q = N((B, H, S, D), 70, dev, torch.float16)
+    k = N((B, H, S, D), 71, dev, torch.float16)
+    v = N((B, H, S, D), 72, dev, torch.float16)
+    ramp = torch.linspace(0.2, 6.0, S, device=dev, dtype=torch.float16).view(1, 1, S, 1)
+    k = (k * ramp).contiguous()
+    q = (q.abs() * 0 + 1.0).to(torch.float16) * torch.sign(k.sum(dim=2, keepdim=True))  # aligned with keys
+    q = q.contiguous()
+    scale = 1.0 / math.sqrt(D)
+    o = ops.fmha(q, k, v, scale, causal)
+    ops.check_device()
+    hq, hk, hv, ho = host(q), host(k), host(v), host(o)
+    for h in range(H):
+        ref = O.fmha(hq[0, h], hk[0, h], hv[0, h], scale, causal)
+        assert np.all(np.isfinite(ho[0, h]))
+        assert O.isapprox(ho[0, h], ref, 1e-2), h
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("causal", [False, True])
 def test_fmha_full_size_sampled(dev, causal):
