@@ -123,7 +123,7 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 // Debug-only timeline of CTA 0 (clock64 cycles): [event][block] where events
 // are 0/1 softmax tile t got S (t = 0, 1), 2/3 softmax tile t arrived P,
 // 4/5 MMA issued P_t*V, 6/7 MMA issued S_t(j+1), 8 MMA got V.
-__device__ long long g_fmha_trace[9][128];
+__device__ long long g_fmha_trace[13][128];  // 9-12: completion of PV0, S0', PV1, S1'
 #define FMHA_TRACE(ev, j)                                                      \
   do {                                                                       \
     if (blockIdx.x == 0 && (j) < 128) g_fmha_trace[(ev)][(j)] = clock64();   \
@@ -154,10 +154,10 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-    mma_f16_ss(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
+    mma_f16_ss_elect(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
                smem_desc_sw128(ka + off, 16, 1024), idesc_s, kk != 0);
   }
-  mma_commit(s_full_t);
+  mma_commit_elect(s_full_t);
 }
 
 // O_t (+)= P_t V for one key block: P_t from TMEM (128 keys packed in S_t
@@ -169,7 +169,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
   const uint32_t va = sVa + stage * TILE_BYTES;
 #pragma unroll
   for (int kk = 0; kk < BKV / 16; ++kk)
-    mma_f16_ts(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
+    mma_f16_ts_elect(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
                smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
                (j > 0 || kk > 0) ? 1u : 0u);
 }
@@ -195,6 +195,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* p_full = bars + 11;  // [2]
   uint64_t* o_full = bars + 13;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+#ifdef CTB_FMHA_TRACE
+  uint64_t* grp_done = bars + 16;  // [4]: trace-only completion of each MMA group
+#endif
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -216,6 +219,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], SM_THREADS_PER_TILE);
       mbar_init(&o_full[i], 1);
+#ifdef CTB_FMHA_TRACE
+      mbar_init(&grp_done[2 * i], 1);
+      mbar_init(&grp_done[2 * i + 1], 1);
+#endif
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -256,15 +263,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    {  // the whole warp runs the issue loop converged; elect.sync issues
       const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, ERR_BIT);
-      if (ok) ok = mbar_wait_bounded(&k_full[0], 0, abort_flag, ERR_BIT);
+      // Wait results are made warp-uniform so the warp never diverges around elect.sync.
+      bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(q_full, 0, abort_flag, ERR_BIT));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[0], 0, abort_flag, ERR_BIT));
       if (ok) {
         tc_fence_after();
         issue_s(tmem, sQa, sKa, 0, 0, &s_full[0]);
         issue_s(tmem, sQa, sKa, 1, 0, &s_full[1]);
-        mma_commit(&k_empty[0]);
+        mma_commit_elect(&k_empty[0]);
       }
       // Tensor-pipe order per key block j: PV0(j) S0(j+1) PV1(j) S1(j+1). The
       // pipe executes one thread's MMAs in issue order, so S_t(j+1) never
@@ -273,32 +281,55 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = j & 1, sn = (j + 1) & 1;
         const uint32_t ph = (j >> 1) & 1, phn = ((j + 1) >> 1) & 1;
         const bool more = j + 1 < nb;
-        if (!(ok = mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT))) break;
-        FMHA_TRACE(8, j);
-        if (!(ok = mbar_wait_bounded(&p_full[0], j & 1, abort_flag, ERR_BIT))) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT)))) break;
+        if (lane == 0) FMHA_TRACE(8, j);
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[0], j & 1, abort_flag, ERR_BIT)))) break;
         tc_fence_after();
         issue_pv(tmem, sVa, 0, s, j);
-        FMHA_TRACE(4, j);
+#ifdef CTB_FMHA_TRACE
+        mma_commit_elect(&grp_done[0]);
+#endif
+        if (lane == 0) FMHA_TRACE(4, j);
         if (more) {
-          if (!(ok = mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT))) break;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
           issue_s(tmem, sQa, sKa, 0, sn, &s_full[0]);
-          FMHA_TRACE(6, j);
+#ifdef CTB_FMHA_TRACE
+        mma_commit_elect(&grp_done[1]);
+#endif
+          if (lane == 0) FMHA_TRACE(6, j);
         }
-        if (!(ok = mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT))) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT)))) break;
         tc_fence_after();
         issue_pv(tmem, sVa, 1, s, j);
-        FMHA_TRACE(5, j);
-        mma_commit(&v_empty[s]);
+#ifdef CTB_FMHA_TRACE
+        mma_commit_elect(&grp_done[2]);
+#endif
+        if (lane == 0) FMHA_TRACE(5, j);
+        mma_commit_elect(&v_empty[s]);
         if (more) {
           issue_s(tmem, sQa, sKa, 1, sn, &s_full[1]);
-          FMHA_TRACE(7, j);
-          mma_commit(&k_empty[sn]);
+#ifdef CTB_FMHA_TRACE
+        mma_commit_elect(&grp_done[3]);
+#endif
+          if (lane == 0) FMHA_TRACE(7, j);
+          mma_commit_elect(&k_empty[sn]);
         }
       }
-      mma_commit(&o_full[0]);
-      mma_commit(&o_full[1]);
+      mma_commit_elect(&o_full[0]);
+      mma_commit_elect(&o_full[1]);
     }
+#ifdef CTB_FMHA_TRACE
+  } else if (warp == 10) {
+    if (lane == 0 && blockIdx.x == 0) {
+      for (int j = 0; j < nb && j < 128; ++j)
+        for (int g = 0; g < 4; ++g) {
+          if ((g == 1 || g == 3) && j + 1 >= nb) continue;
+          if (!mbar_wait_bounded(&grp_done[g], j & 1, abort_flag, ERR_BIT)) break;
+          g_fmha_trace[9 + g][j] = clock64();
+        }
+    }
+#endif
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax warpgroups
     // One thread per query row, all 128 scores of a block in registers.
