@@ -160,18 +160,21 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
   mma_commit_elect(s_full_t);
 }
 
-// O_t (+)= P_t V for one key block: P_t from TMEM (128 keys packed in S_t
+// O_t (+)= P_t V for one half (64 keys) of a key block: P_t from TMEM (128 keys packed in S_t
 // columns 0-63; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
 // 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
-__device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j) {
+__device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j,
+                                         int half) {
   using namespace sm100;
   constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
   const uint32_t va = sVa + stage * TILE_BYTES;
 #pragma unroll
-  for (int kk = 0; kk < BKV / 16; ++kk)
+  for (int k4 = 0; k4 < BKV / 32; ++k4) {
+    const int kk = half * (BKV / 32) + k4;
     mma_f16_ts_elect(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
-               smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
-               (j > 0 || kk > 0) ? 1u : 0u);
+                     smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+  }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -192,7 +195,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;  // [2]
+  uint64_t* p_full = bars + 20;  // [2 tiles][2 halves of the keys]
   uint64_t* o_full = bars + 13;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 #ifdef CTB_FMHA_TRACE
@@ -217,7 +220,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], SM_THREADS_PER_TILE);
+      mbar_init(&p_full[2 * i], SM_THREADS_PER_TILE);
+      mbar_init(&p_full[2 * i + 1], SM_THREADS_PER_TILE);
       mbar_init(&o_full[i], 1);
 #ifdef CTB_FMHA_TRACE
       mbar_init(&grp_done[2 * i], 1);
@@ -283,9 +287,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool more = j + 1 < nb;
         if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT)))) break;
         if (lane == 0) FMHA_TRACE(8, j);
+        // P*V on the first 64 keys starts while the softmax finishes the rest.
         if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[0], j & 1, abort_flag, ERR_BIT)))) break;
         tc_fence_after();
-        issue_pv(tmem, sVa, 0, s, j);
+        issue_pv(tmem, sVa, 0, s, j, 0);
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT)))) break;
+        tc_fence_after();
+        issue_pv(tmem, sVa, 0, s, j, 1);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[0]);
 #endif
@@ -299,9 +307,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
           if (lane == 0) FMHA_TRACE(6, j);
         }
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT)))) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[2], j & 1, abort_flag, ERR_BIT)))) break;
         tc_fence_after();
-        issue_pv(tmem, sVa, 1, s, j);
+        issue_pv(tmem, sVa, 1, s, j, 0);
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[3], j & 1, abort_flag, ERR_BIT)))) break;
+        tc_fence_after();
+        issue_pv(tmem, sVa, 1, s, j, 1);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[2]);
 #endif
@@ -381,12 +392,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_use = m_blk;
         rescale = true;
       }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_t is stable here: P_t*V of block j-1 completed before S_t of block j,
+        // and P_t*V of block j waits for this thread's p_full arrivals below.
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld_32x32b_x16(o_col + c * 16, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st_32x32b_x16(o_col + c * 16, o);
+        }
+      }
       // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
       // (-inf) - (-inf) would be NaN, so shift by 0 for them.
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
       const uint64_t sl2x2 = f2_pack(sl2, sl2), nm2 = f2_pack(-mref, -mref);
       uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
-      // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read above.
+      // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read
+      // above. Each half (keys 0-63, 64-127) is published as soon as it is stored.
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -409,27 +434,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           pk[i] = pack_half2(ea, eb);
         }
         tmem_st_32x32b_x16(s_col + c * 16, pk);
+        if (c & 1) {
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(&p_full[t * 2 + (c >> 1)]);
+        }
       }
       float s0, s1, s2, s3;
       f2_unpack(acc0, s0, s1);
       f2_unpack(acc1, s2, s3);
       l += (s0 + s1) + (s2 + s3);
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_t is stable here: P_t*V of block j-1 completed before S_t of block j,
-        // and P_t*V of block j waits for this thread's p_full arrival below.
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(o_col + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          tmem_st_32x32b_x32(o_col + c * 32, o);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
       if (threadIdx.x % 128 == 0) FMHA_TRACE(2 + t, j);
     }
     // ------------------------------------------------------------ epilogue
