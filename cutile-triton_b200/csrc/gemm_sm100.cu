@@ -125,39 +125,43 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp runs the loop converged (descriptors stay warp-uniform)
+    // and elect.sync picks the issuing lane; wait results are made uniform.
+    {
       constexpr uint32_t idesc = idesc_f16_f32(BM, BN, /*a MN-major*/ true, /*b K-major*/ false);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int64_t t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++it) {
         const int buf = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait_bounded(&tmem_empty[buf], acc_phase ^ 1, abort_flag, ERR_BIT)) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tmem_empty[buf], acc_phase ^ 1, abort_flag, ERR_BIT)))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, ERR_BIT)) break;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[stage], phase, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t sb = sa + A_STAGE_BYTES;
+          // A, MN-major SW128: LBO = 8 KB between the two 64-row halves,
+          // SBO = 1 KB between 8-k-row groups; K step of 16 = 2 KB.
+          const uint64_t ad = smem_desc_sw128(sa, A_HALF_BYTES, 1024);
+          // B, K-major SW128: SBO = 1 KB between 8-row groups; K step of 16
+          // halves = 32 bytes inside the swizzled 128-byte row. Steps are
+          // added to the (address >> 4) field.
+          const uint64_t bd = smem_desc_sw128(sa + A_STAGE_BYTES, 16, 1024);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // A, MN-major SW128: LBO = 8 KB between the two 64-row halves,
-            // SBO = 1 KB between 8-k-row groups; K step of 16 = 2 KB.
-            const uint64_t ad = smem_desc_sw128(sa + k * 2048, A_HALF_BYTES, 1024);
-            // B, K-major SW128: SBO = 1 KB between 8-row groups; K step of
-            // 16 halves = 32 bytes inside the swizzled 128-byte row.
-            const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
-            mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0);
-          }
-          mma_commit(&empty[stage]);  // frees the stage when these MMAs finish
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_ss_elect(d_tmem, ad + (uint64_t)(k * 2048 >> 4), bd + (uint64_t)(k * 32 >> 4),
+                             idesc, (kb | k) != 0);
+          mma_commit_elect(&empty[stage]);  // frees the stage when these MMAs finish
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        mma_commit(&tmem_full[buf]);  // accumulator ready for the epilogue
+        if (!ok) break;
+        mma_commit_elect(&tmem_full[buf]);  // accumulator ready for the epilogue
       }
     }
   } else {
