@@ -61,11 +61,13 @@ def _wl():
                  4 * 8 * 32 * S * S * 128),
         "fmha_causal": ("fmha fwd f16 B8 H32 S8192 D128 causal", "TFLOP/s", "tensor",
                         2 * 8 * 32 * S * S * 128),
+        "moe": ("fused-MoE f16 GEMM, 16384 tokens, top-2 of 8 experts, N=14336, K=4096 "
+                "(extra: not a BASELINE config)", "TFLOP/s", "tensor", 2 * 16384 * 2 * 14336 * 4096),
     }
 
 
 WORKLOADS = _wl()
-SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "transpose", "gemm", "bgemm", "fmha", "fmha_causal"]
+SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "transpose", "gemm", "bgemm", "fmha", "fmha_causal", "moe"]
 
 
 def load_peaks():
@@ -170,6 +172,18 @@ class Case:
             causal = name == "fmha_causal"
             self.run = lambda: ops.fmha(q, k, v, 1.0 / math.sqrt(128), causal, o)
             self.inputs, self.outputs = [q, k, v], [o]
+        elif name == "moe":
+            M, E, topk, N, K = (4096 if small else 16384), 8, 2, 14336, 4096
+            A = ops.fill_uniform(T.empty(M, K, dtype=T.float16, device=dev), seed)
+            B = ops.fill_uniform(T.empty(E, N, K, dtype=T.float16, device=dev), seed + 1,
+                                 -0.05, 0.05)
+            g = T.Generator().manual_seed(seed)
+            ids = T.argsort(T.rand(M, E, generator=g), dim=1)[:, :topk].to(T.int32).to(dev)
+            w = T.rand(M, topk, generator=g).to(dev)
+            sid, eid, ntp = ops.moe_align(ids, E)
+            C = T.empty(M * topk, N, dtype=T.float16, device=dev)
+            self.run = lambda: ops.moe_gemm(A, B, sid, eid, ntp, topk, w, C)
+            self.inputs, self.outputs = [A, B, sid, eid, ntp, w], [C]
         else:
             raise ValueError(name)
 
@@ -444,6 +458,20 @@ def cpu_measure(name, budget_s):
         v = loop(lambda: A @ B, 2 * s ** 3) / 1e12
         return v, (f"numpy/OpenBLAS sgemm {s}^3 on Float32 copies (Julia's Float16 mul! is "
                    f"generic code), repeated for {budget_s:.0f} s"), threads
+    if name == "moe":
+        T, K, N, E, topk = 1024, 4096, 2048, 8, 2
+        A = rng.uniform(-1, 1, (T, K)).astype(np.float32)
+        B = rng.uniform(-1, 1, (E, N, K)).astype(np.float32)
+        ids = np.stack([rng.choice(E, topk, replace=False) for _ in range(T)])
+        groups = [np.nonzero((ids == e).any(axis=1))[0] for e in range(E)]
+
+        def one():
+            for e in range(E):
+                A[groups[e]] @ B[e].T
+
+        v = loop(one, 2 * T * topk * N * K) / 1e12
+        return v, (f"{T} tokens, top-{topk} of {E} experts, N={N} of 14336, K={K}: per-expert "
+                   f"gather + numpy/OpenBLAS sgemm, repeated for {budget_s:.0f} s"), threads
     if name in ("fmha", "fmha_causal"):
         S, D = 2048, 128
         q = rng.standard_normal((S, D)).astype(np.float32)

@@ -128,6 +128,7 @@ int gemm_device_setup();
 int fmha_device_setup();
 int gemm_take_device_error(unsigned int* out);
 int fmha_take_device_error(unsigned int* out);
+int moe_take_device_error(unsigned int* out);
 }
 
 extern "C" int ctb_init(int device) {
@@ -153,7 +154,9 @@ extern "C" int ctb_check_device(void* stream) {
   unsigned int hg = 0, hf = 0;
   if (int e = gemm_take_device_error(&hg)) return cuda_fail((cudaError_t)e, "reading the GEMM error word");
   if (int e = fmha_take_device_error(&hf)) return cuda_fail((cudaError_t)e, "reading the FMHA error word");
-  const unsigned int h = hg | hf;
+  unsigned int hm = 0;
+  if (int e = moe_take_device_error(&hm)) return cuda_fail((cudaError_t)e, "reading the MoE error word");
+  const unsigned int h = hg | hf | hm;
   if (h) {
     return set_error(CTB_ERR_TIMEOUT, "a bounded device-side wait gave up (error word " +
                                           std::to_string(h) + ")");

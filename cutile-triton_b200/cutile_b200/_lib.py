@@ -86,6 +86,9 @@ SIGNATURES = {
     "ctb_bgemm_f16": [_P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64,
                       _P],
     "ctb_fmha_fwd_f16": [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P],
+    "ctb_moe_workspace_bytes": [_I32, _I32],
+    "ctb_moe_gemm_f16": [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
+                         _I64, _I64, _I64, _P, _I64, _P],
     "ctb_fill_uniform": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
     "ctb_fill_normal": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
 }
@@ -111,6 +114,7 @@ def load():
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int
+    L.ctb_moe_workspace_bytes.restype = ctypes.c_int64
     L.ctb_last_error.argtypes = []
     L.ctb_last_error.restype = ctypes.c_char_p
     _lib = L

@@ -185,3 +185,65 @@ def fmha(q, k, v, scale, causal=False, out=None):
     _lib.call("ctb_fmha_fwd_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, H,
               Sq, Sk, D, ctypes.c_float(scale), 1 if causal else 0, _st())
     return out
+
+
+MOE_BLOCK = 128
+
+
+def moe_align(topk_ids, num_experts, block=MOE_BLOCK):
+    """Routing in the fused-MoE layout: returns (sorted_token_ids int32 [EM],
+    expert_ids int32 [EM/block], num_tokens_post_padded int32 [1]) on the
+    device of `topk_ids` ((M, topk) int tensor). Slots of each expert are
+    listed in token order and padded to a multiple of `block` with M*topk."""
+    flat = topk_ids.reshape(-1).to(torch.int64)
+    n = flat.numel()
+    counts = torch.bincount(flat, minlength=num_experts)
+    padded = (counts + block - 1) // block * block
+    em = int(padded.sum().item())
+    order = torch.argsort(flat * n + torch.arange(n, device=flat.device))  # stable by expert
+    sorted_ids = torch.full((max(em, block),), n, dtype=torch.int32, device=flat.device)
+    starts = torch.cumsum(padded, 0) - padded
+    cstarts = torch.cumsum(counts, 0) - counts
+    pos = starts[flat[order]] + (torch.arange(n, device=flat.device) - cstarts[flat[order]])
+    sorted_ids[pos] = order.to(torch.int32)
+    expert_ids = torch.repeat_interleave(torch.arange(num_experts, device=flat.device),
+                                         padded // block).to(torch.int32)
+    if expert_ids.numel() * block < sorted_ids.numel():
+        expert_ids = torch.cat([expert_ids, torch.full((1,), -1, dtype=torch.int32,
+                                                       device=flat.device)])
+    ntp = torch.tensor([em], dtype=torch.int32, device=flat.device)
+    return sorted_ids, expert_ids, ntp
+
+
+_moe_ws = {}
+
+
+def moe_workspace(EM, K, device):
+    """The routed-rows workspace for ctb_moe_gemm_f16, cached per device and
+    grown on demand (EM x K Float16)."""
+    need = int(_lib.load().ctb_moe_workspace_bytes(EM, K))
+    key = torch.device(device)
+    ws = _moe_ws.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 16), dtype=torch.uint8, device=key)
+        _moe_ws[key] = ws
+    return ws
+
+
+def moe_gemm(A, B, sorted_ids, expert_ids, ntp, topk, weights=None, out=None, workspace=None):
+    """Fused-MoE GEMM: A (M, K) f16, B (E, N, K) f16 -> C (M*topk, N) f16 with
+    C[s] = A[s // topk] @ B[e].T (* weights[s]) for the slots s routed to e.
+    Rows of C that no block in use lists are left as they were."""
+    _need_cuda(A, B, sorted_ids, expert_ids, ntp)
+    M, K = A.shape
+    E, N, _ = B.shape
+    EM = sorted_ids.numel()
+    out = torch.zeros(M * topk, N, dtype=A.dtype, device=A.device) if out is None else out
+    w = weights.reshape(-1).contiguous() if weights is not None else None
+    ws = moe_workspace(EM, K, A.device) if workspace is None else workspace
+    _lib.call("ctb_moe_gemm_f16", A.data_ptr(), B.data_ptr(), out.data_ptr(),
+              sorted_ids.data_ptr(), expert_ids.data_ptr(), ntp.data_ptr(),
+              w.data_ptr() if w is not None else None, 1 if w is not None else 0,
+              M, N, K, E, EM, topk, A.stride(0), B.stride(1), out.stride(0),
+              ws.data_ptr(), ws.numel() * ws.element_size(), _st())
+    return out

@@ -218,6 +218,28 @@ int ctb_fmha_fwd_f16(const void* Q, const void* K, const void* V, void* O,
                      int32_t seq_k, int32_t head_dim, float scale,
                      int32_t causal, void* stream);
 
+/* Gather-routed mixture-of-experts GEMM (the cuTile moe example is not
+ * vendored in the reference; research/bench_final.log:7 benchmarks it). The
+ * contract is the published fused-MoE one: `sorted_token_ids` (EM entries,
+ * EM a multiple of 128) lists token*topk slots grouped by expert, each expert
+ * padded to a multiple of 128 with ids >= M*topk; `expert_ids[EM/128]` gives
+ * each 128-block's expert; `*num_tokens_post_padded` (device int) bounds the
+ * blocks in use. For every listed slot s < M*topk of a block of expert e:
+ *   C[s, :] = (A[s / topk, :] . B[e]^T) * (mul_routed_weight ? w[s] : 1)
+ * A: M x K Float16 row-major (row stride lda); B: E x N x K Float16, K
+ * contiguous (row stride ldb, expert stride N*ldb); C: (M*topk) x N Float16
+ * row-major (ldc); Float32 accumulation. K, lda, ldb, ldc multiples of 8.
+ * `workspace` (16-byte aligned, at least ctb_moe_workspace_bytes(EM, K))
+ * receives the routed rows of A in sorted order before the GEMM runs. */
+int64_t ctb_moe_workspace_bytes(int32_t EM, int32_t K);
+int ctb_moe_gemm_f16(const void* A, const void* B, void* C,
+                     const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                     const int32_t* num_tokens_post_padded,
+                     const float* topk_weights, int32_t mul_routed_weight,
+                     int32_t M, int32_t N, int32_t K, int32_t E, int32_t EM,
+                     int32_t topk, int64_t lda, int64_t ldb, int64_t ldc,
+                     void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ---- seeded synthetic inputs (bench / test plumbing, not a cuTile op) ---- */
 
 /* Counter-based SplitMix64 stream: element i uses counter offset + i.

@@ -14,7 +14,7 @@ layernorm with OpenMP; GEMM and attention are restated here in numpy float64
 * matmul:   ``Float32.(A) * Float32.(B)``; error = max|got-ref| / max|ref|
             bench/bench_f16.jl:27, 49-50; test/runtests.jl:95-98
 * isapprox: Julia ``≈`` = norm(x-y) <= rtol*max(norm(x), norm(y))
-* layernorm fwd/bwd / batchmatmul / fmha: the cuTile examples are not vendored in the
+* layernorm fwd/bwd / batchmatmul / fmha / moe: the cuTile examples are not vendored in the
   reference (parity unpinned); restated from their standard definitions.
 """
 import ctypes
@@ -206,6 +206,50 @@ def fmha(q, k, v, scale, causal=False, rows=None):
     p = np.exp(s)
     p /= p.sum(axis=1, keepdims=True)
     return p @ v
+
+
+def moe_align(topk_ids, num_experts, block=128):
+    """Fused-MoE routing restated with plain loops: slots (token*topk + j) of
+    each expert in slot order, each expert padded to a multiple of `block`
+    with the id M*topk; returns (sorted_ids, expert_ids, num_post_padded)."""
+    flat = np.asarray(topk_ids, np.int64).ravel()
+    n = flat.size
+    sorted_ids, expert_ids = [], []
+    for e in range(num_experts):
+        slots = [s for s in range(n) if flat[s] == e]
+        pad = (-len(slots)) % block
+        sorted_ids += slots + [n] * pad
+        expert_ids += [e] * ((len(slots) + pad) // block)
+    em = len(sorted_ids)
+    if em == 0:
+        sorted_ids, expert_ids = [n] * block, [-1]
+    return (np.asarray(sorted_ids, np.int32), np.asarray(expert_ids, np.int32), em)
+
+
+def moe(A, B, sorted_ids, expert_ids, num_post_padded, topk, weights=None, block=128):
+    """Float64 fused-MoE GEMM: rows C[s] = A[s // topk] @ B[e].T (* weights[s])
+    for each listed slot s < M*topk of a block (below num_post_padded) of a
+    valid expert e; rows never listed stay zero. A (M, K); B (E, N, K)."""
+    A = np.asarray(A, np.float64)
+    B = np.asarray(B, np.float64)
+    M = A.shape[0]
+    E, N, _ = B.shape
+    w = None if weights is None else np.asarray(weights, np.float64).ravel()
+    C = np.zeros((M * topk, N))
+    nblk = min(len(expert_ids), (int(num_post_padded) + block - 1) // block)
+    for b in range(nblk):
+        e = int(expert_ids[b])
+        if not 0 <= e < E:
+            continue
+        ids = np.asarray(sorted_ids[b * block:(b + 1) * block], np.int64)
+        ids = ids[(ids >= 0) & (ids < M * topk)]
+        if ids.size == 0:
+            continue
+        rows = A[ids // topk] @ B[e].T
+        if w is not None:
+            rows *= w[ids][:, None]
+        C[ids] = rows
+    return C
 
 
 # ---- float-accumulating variants: the timed CPU baseline ------------------------

@@ -1,0 +1,94 @@
+"""Parity of the gather-routed MoE GEMM (ctb_moe_gemm_f16) against the float64
+oracle. Tolerance: relative Frobenius error <= 2e-3 (the f16 GEMM bound), and
+rows that no block lists must be left untouched (exactly as preset)."""
+import numpy as np
+import pytest
+import torch
+
+from cutile_b200 import ops
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def routing(M, E, topk, seed, skew=False):
+    g = torch.Generator().manual_seed(seed)
+    r = torch.rand(M, E, generator=g)
+    if skew:  # expert 0 never chosen, expert 1 almost always
+        r[:, 0] = -1.0
+        r[:, 1] += 1.0
+    return torch.argsort(r, dim=1, descending=True)[:, :topk].to(torch.int32)
+
+
+def make(dev, M, N, K, E, seed):
+    A = torch.empty(M, K, dtype=torch.float16, device=dev)
+    B = torch.empty(E, N, K, dtype=torch.float16, device=dev)
+    ops.fill_uniform(A, seed, -1.0, 1.0)
+    ops.fill_uniform(B, seed + 1, -1.0, 1.0)
+    return A, B
+
+
+@pytest.mark.parametrize("M,N,K,E,topk,weighted,skew", [
+    (64, 256, 128, 4, 2, False, False),
+    (300, 200, 136, 7, 3, True, False),
+    (1000, 512, 64, 8, 2, True, True),
+    (5, 64, 8, 3, 1, False, False),
+    (2048, 768, 512, 16, 4, True, False),
+])
+def test_moe_gemm(dev, M, N, K, E, topk, weighted, skew):
+    A, B = make(dev, M, N, K, E, 21 + M)
+    ids = routing(M, E, topk, M, skew)
+    sid, eid, ntp = ops.moe_align(ids.to(dev), E)
+    w = torch.rand(M, topk, generator=torch.Generator().manual_seed(3)).to(dev) if weighted else None
+    C = ops.moe_gemm(A, B, sid, eid, ntp, topk, w)
+    torch.cuda.synchronize()
+    ref = O.moe(A.cpu().numpy(), B.cpu().numpy(), sid.cpu().numpy(), eid.cpu().numpy(),
+                int(ntp.item()), topk, None if w is None else w.cpu().numpy())
+    got = C.cpu().numpy().astype(np.float64)
+    assert O.rel_fro(got, ref) <= 2e-3
+    assert np.all(np.isfinite(got))
+
+
+def test_moe_align_matches_oracle_loops(dev):
+    ids = routing(333, 9, 3, 5, skew=True)
+    s, e, n = ops.moe_align(ids.to(dev), 9)
+    rs, re, rn = O.moe_align(ids.numpy(), 9)
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+    np.testing.assert_array_equal(e.cpu().numpy(), re)
+    assert int(n.item()) == rn
+
+
+def test_moe_unlisted_rows_and_invalid_blocks_untouched(dev):
+    """Blocks past num_tokens_post_padded and blocks with expert id -1 are
+    skipped; the rows they list keep their preset value."""
+    M, N, K, E, topk = 256, 256, 128, 2, 1
+    A, B = make(dev, M, N, K, E, 7)
+    sid = torch.arange(M, dtype=torch.int32, device=dev)            # 2 blocks of 128
+    eid = torch.tensor([-1, 1], dtype=torch.int32, device=dev)
+    ntp = torch.tensor([M], dtype=torch.int32, device=dev)
+    out = torch.full((M, N), 3.0, dtype=torch.float16, device=dev)
+    ops.moe_gemm(A, B, sid, eid, ntp, topk, out=out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.all(got[:128] == 3.0)
+    ref = A.cpu().double()[128:] @ B.cpu().double()[1].T
+    assert O.rel_fro(got[128:], ref.numpy()) <= 2e-3
+    # num_tokens_post_padded below EM: the second block is no longer in use
+    out.fill_(3.0)
+    ntp.fill_(128)
+    eid[0] = 0
+    ops.moe_gemm(A, B, sid, eid, ntp, topk, out=out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.all(got[128:] == 3.0)
+    assert O.rel_fro(got[:128], (A.cpu().double()[:128] @ B.cpu().double()[0].T).numpy()) <= 2e-3
+
+
+def test_moe_bad_layout_reported(dev):
+    A = torch.zeros(16, 12, dtype=torch.float16, device=dev)  # K % 8 != 0
+    B = torch.zeros(2, 64, 12, dtype=torch.float16, device=dev)
+    sid = torch.zeros(128, dtype=torch.int32, device=dev)
+    eid = torch.zeros(1, dtype=torch.int32, device=dev)
+    ntp = torch.tensor([128], dtype=torch.int32, device=dev)
+    with pytest.raises(Exception):
+        ops.moe_gemm(A, B, sid, eid, ntp, 1)
