@@ -67,6 +67,7 @@ def _wl():
 
 
 WORKLOADS = _wl()
+LAUNCHES_PER_STEP = {"layernorm_bwd": 2, "moe": 2}  # row pass + fold; row gather + GEMM
 SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "transpose", "gemm", "bgemm", "fmha", "fmha_causal", "moe"]
 
 
@@ -588,7 +589,10 @@ def run_ours(args):
         value = world * work * steps / (total_ms * 1e-3) / scale
         res = {"value": round(value, 3), "unit": unit, "ms_per_step": round(total_ms / steps, 5),
                "roofline": roofline(name, mean_ms, peaks, peak_src, traffic),
-               "gpu_launches": steps}
+               "gpu_launches": steps * LAUNCHES_PER_STEP.get(name, 1),
+               "dtype": "f16" if bound == "tensor" else "f32",
+               "l2": (f"inputs larger than L2 (126 MB): {case.bytes_in() / 1e6:.0f} MB read + "
+                      f"{case.bytes_out() / 1e6:.0f} MB written per step")}
         if want_e2e:
             k = max(2, min(steps, 10))
             ms, bi, bo = time_e2e(case, k, dev, dist_on)
@@ -623,11 +627,11 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": h["value"], "unit": h["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": h["ms_per_step"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": h["dtype"],
             "data": "synthetic (seeded SplitMix64, BASELINE shapes and distributions)",
-            "config": {"workload": desc, "config_index": 1,
+            "config": {"workload": desc, "config_index": 1 if head == "softmax" else None,
                        "parallelism": f"dp{world} (rows; weak scaling, each rank a full config)",
-                       "l2": "inputs larger than L2 (126 MB): 268 MB read + 268 MB written per step"},
+                       "l2": h["l2"]},
             "roofline": h["roofline"], "cpu_baseline": h.get("cpu_baseline"),
             "e2e": h.get("e2e"), "gpu_launches": h["gpu_launches"], "clocks": clocks,
             "library": cutile_b200.library_path(), "suite": suite, "launch_path": lp,
@@ -651,7 +655,7 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     ops.init(0)
-    case = Case(args.profile, dev, 0, small=True)
+    case = Case(args.profile, dev, 0, small=not args.full_size)
     for _ in range(args.warmup + args.steps):
         case.run()
     torch.cuda.synchronize()
@@ -673,6 +677,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU work for the headline cpu_baseline")
     ap.add_argument("--ref-budget", type=float, default=15.0)
+    ap.add_argument("--full-size", action="store_true",
+                    help="with --profile: the bench's own sizes instead of the small case")
     ap.add_argument("--profile", default=None, choices=list(WORKLOADS),
                     help="launch-only mode for ncu captures")
     args = ap.parse_args()

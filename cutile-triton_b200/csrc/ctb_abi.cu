@@ -417,6 +417,47 @@ int L_fmha(const ctb_array* x, const double* s, cudaStream_t st) {
                           s[1] != 0.0 ? 1 : 0, st);
 }
 
+// moe(A, B, C, SORTED, EXPERT_IDS, NTP, WEIGHTS, WORKSPACE, topk, mul_routed_weight):
+// Julia arrays A (K, M), B (K, N, E), C (N, M*topk) Float16 with contiguous
+// first dims (B's experts N*ldb apart); SORTED (EM), EXPERT_IDS (EM/128), NTP
+// (>= 1) Int32; WEIGHTS Float32 (topk, M) contiguous; WORKSPACE Float16
+// holding at least K*EM elements.
+int L_moe(const ctb_array* x, const double* s, cudaStream_t st) {
+  const ctb_array &A = x[0], &B = x[1], &C = x[2], &S = x[3], &EI = x[4], &NT = x[5],
+                  &W = x[6], &WS = x[7];
+  if (int rc = need_dims(A, 2, "moe", "A")) return rc;
+  if (int rc = need_dims(B, 3, "moe", "B")) return rc;
+  if (int rc = need_dims(C, 2, "moe", "C")) return rc;
+  if (int rc = need_dims(S, 1, "moe", "sorted_token_ids")) return rc;
+  if (int rc = need_dims(EI, 1, "moe", "expert_ids")) return rc;
+  if (int rc = need_dims(NT, 1, "moe", "num_tokens_post_padded")) return rc;
+  if (A.dtype != CTB_F16 || B.dtype != CTB_F16 || C.dtype != CTB_F16 || WS.dtype != CTB_F16)
+    return set_error(CTB_ERR_DTYPE, "moe: A, B, C and the workspace must be Float16");
+  if (S.dtype != CTB_I32 || EI.dtype != CTB_I32 || NT.dtype != CTB_I32)
+    return set_error(CTB_ERR_DTYPE, "moe: routing tables must be Int32");
+  const int topk = (int)s[0], mul = s[1] != 0.0 ? 1 : 0;
+  if (mul && W.dtype != CTB_F32) return set_error(CTB_ERR_DTYPE, "moe: weights must be Float32");
+  const int K = A.sizes[0], M = A.sizes[1], N = B.sizes[1], E = B.sizes[2], EM = S.sizes[0];
+  if (B.sizes[0] != K || C.sizes[0] != N || (int64_t)C.sizes[1] != (int64_t)M * topk ||
+      NT.sizes[0] < 1 || (int64_t)EI.sizes[0] * 128 < EM)
+    return set_error(CTB_ERR_SHAPE, "moe: A/B/C/routing sizes disagree");
+  if (A.strides[0] != 1 || B.strides[0] != 1 || C.strides[0] != 1 || S.strides[0] != 1 ||
+      EI.strides[0] != 1 || (int64_t)B.strides[2] != (int64_t)B.strides[1] * N)
+    return set_error(CTB_ERR_LAYOUT, "moe: first dims must be contiguous, B's experts packed");
+  int64_t ws_elems = 1;
+  for (int d = 0; d < WS.ndim; ++d) ws_elems *= WS.sizes[d];
+  if (mul) {
+    int64_t w_elems = 1;
+    for (int d = 0; d < W.ndim; ++d) w_elems *= W.sizes[d];
+    if (w_elems < (int64_t)M * topk || W.strides[0] != 1)
+      return set_error(CTB_ERR_SHAPE, "moe: weights need topk x M contiguous Float32");
+  }
+  return ctb_moe_gemm_f16(A.ptr, B.ptr, C.ptr, (const int32_t*)S.ptr, (const int32_t*)EI.ptr,
+                          (const int32_t*)NT.ptr, mul ? (const float*)W.ptr : nullptr, mul, M,
+                          N, K, E, EM, topk, A.strides[1], B.strides[1], C.strides[1], WS.ptr,
+                          ws_elems * 2, st);
+}
+
 const Entry kRegistry[] = {
     {"vadd", 3, 0, 8, 0, L_vadd},
     {"rowsum", 2, 0, 16, 0, L_rowsum},
@@ -430,10 +471,11 @@ const Entry kRegistry[] = {
     {"batch_matmul", 3, 0, 6, 0, L_bmm},
     {"fmha", 4, 2, 16, 0, L_fmha},
     {"transpose", 2, 0, 8, 0, L_transpose},
+    {"moe", 8, 2, 6, 0, L_moe},
 };
 constexpr int kRegistrySize = sizeof(kRegistry) / sizeof(kRegistry[0]);
 
-bool dtype_known(int32_t d) { return d >= CTB_F16 && d <= CTB_F64; }
+bool dtype_known(int32_t d) { return d >= CTB_F16 && d <= CTB_I32; }
 
 }  // namespace
 

@@ -26,7 +26,6 @@
 #include "sm100_ptx.cuh"
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 
 namespace ctb {
@@ -328,8 +327,7 @@ extern "C" int ctb_moe_gemm_f16(const void* A, const void* B, void* C,
   p.tiles_n = (N + moe::BN - 1) / moe::BN;
   p.num_kb = (K + moe::BK - 1) / moe::BK;
   p.num_mblk = EM / moe::BM;
-  p.group_m = 32;
-  if (const char* g = getenv("CTB_MOE_GROUP_M")) p.group_m = std::max(1, atoi(g));
+  p.group_m = 32;  // best of 1..300 on the 8-expert top-2 workload
   const int64_t max_tiles = (int64_t)p.num_mblk * p.tiles_n;
   const int grid = (int)std::min<int64_t>(max_tiles, pr.sm_count);
   moe::moe_gather_rows_kernel<<<EM, 128, 0, static_cast<cudaStream_t>(stream)>>>(

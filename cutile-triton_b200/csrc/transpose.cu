@@ -112,6 +112,8 @@ extern "C" int ctb_transpose(int32_t dtype, const void* x, void* y, int32_t M, i
     case CTB_F32: return launch_transpose((const float*)x, (float*)y, M, N, ldx, ldy, st);
     case CTB_F16: return launch_transpose((const __half*)x, (__half*)y, M, N, ldx, ldy, st);
     case CTB_F64: return launch_transpose((const double*)x, (double*)y, M, N, ldx, ldy, st);
-    default: return set_error(CTB_ERR_DTYPE, "transpose: dtype must be F16, F32 or F64");
+    case CTB_I32:  // moved bit for bit like Float32
+      return launch_transpose((const float*)x, (float*)y, M, N, ldx, ldy, st);
+    default: return set_error(CTB_ERR_DTYPE, "transpose: dtype must be F16, F32, F64 or I32");
   }
 }

@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 DEFAULT_LIB = os.path.join(HERE, "libcutile_b200.so")
 
 CTB_MAX_DIMS = 5
-CTB_F16, CTB_BF16, CTB_F32, CTB_F64 = 1, 2, 3, 4
+CTB_F16, CTB_BF16, CTB_F32, CTB_F64, CTB_I32 = 1, 2, 3, 4, 5
 
 STATUS = {
     0: "CTB_OK",

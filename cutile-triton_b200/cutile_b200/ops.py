@@ -16,7 +16,7 @@ from . import _lib
 from .runtime import current_stream_handle
 
 _DT = {torch.float16: _lib.CTB_F16, torch.bfloat16: _lib.CTB_BF16, torch.float32: _lib.CTB_F32,
-       torch.float64: _lib.CTB_F64}
+       torch.float64: _lib.CTB_F64, torch.int32: _lib.CTB_I32}
 
 
 def _st():

@@ -33,6 +33,7 @@ _DTYPES = {
     torch.bfloat16: _lib.CTB_BF16,
     torch.float32: _lib.CTB_F32,
     torch.float64: _lib.CTB_F64,
+    torch.int32: _lib.CTB_I32,
 }
 
 

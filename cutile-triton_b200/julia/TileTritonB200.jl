@@ -69,6 +69,7 @@ end
 dtype_code(::Type{Float16}) = Int32(1)
 dtype_code(::Type{Float32}) = Int32(3)
 dtype_code(::Type{Float64}) = Int32(4)
+dtype_code(::Type{Int32}) = Int32(5)
 dtype_code(T::Type) = T === ct.TFloat32 ? error("b200: tf32 inputs are stored as Float32 arrays") :
                       (nameof(T) === :BFloat16 ? Int32(2) : error("b200: unsupported element type $T"))
 

@@ -46,7 +46,8 @@ typedef enum {
   CTB_F16 = 1,
   CTB_BF16 = 2,
   CTB_F32 = 3,
-  CTB_F64 = 4
+  CTB_F64 = 4,
+  CTB_I32 = 5 /* Int32: routing tables (moe) */
 } ctb_dtype;
 
 /* One cuTile TileArray after flattening: pointer, sizes, strides (Julia dim

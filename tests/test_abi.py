@@ -42,7 +42,7 @@ def test_version_matches_header():
 
 @pytest.mark.parametrize("name,n", [("vadd", 3), ("rowsum", 2), ("softmax", 2),
                                     ("layernorm_fwd", 6), ("layer_norm_fwd", 6), ("layernorm_bwd", 9), ("matmul", 3),
-                                    ("matmul16", 3), ("batchmatmul", 3), ("fmha", 4), ("transpose", 2)])
+                                    ("matmul16", 3), ("batchmatmul", 3), ("fmha", 4), ("transpose", 2), ("moe", 8)])
 def test_registry_knows_the_seven_kernels(name, n):
     L = _lib.load()
     dt = (ctypes.c_int32 * n)(*([_lib.CTB_F32] * n))
@@ -56,7 +56,7 @@ def test_registry_knows_the_seven_kernels(name, n):
 def test_unknown_kernel_is_an_error_not_a_fallback():
     L = _lib.load()
     h = ctypes.c_int32(-1)
-    rc = L.ctb_find_kernel(b"moe", None, 0, None, 0, ctypes.byref(h))
+    rc = L.ctb_find_kernel(b"fft", None, 0, None, 0, ctypes.byref(h))
     assert rc == -5
     assert b"no prebuilt sm_100a kernel" in L.ctb_last_error()
 
@@ -93,5 +93,5 @@ def test_typed_entry_points_reject_bad_sizes_without_gpu():
 
 def test_python_error_carries_status():
     with pytest.raises(cutile_b200.B200Error) as e:
-        cutile_b200.triton_kernel("moe", [cutile_b200.TileArray(__import__("torch").float32, 1)])
+        cutile_b200.triton_kernel("fft", [cutile_b200.TileArray(__import__("torch").float32, 1)])
     assert e.value.status == "CTB_ERR_UNKNOWN_KERNEL"

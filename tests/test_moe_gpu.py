@@ -92,3 +92,34 @@ def test_moe_bad_layout_reported(dev):
     ntp = torch.tensor([128], dtype=torch.int32, device=dev)
     with pytest.raises(Exception):
         ops.moe_gemm(A, B, sid, eid, ntp, 1)
+
+
+def test_moe_through_the_registry(dev):
+    """triton_kernel("moe", ...) / launch with TileArrays in cuTile order, as
+    the TileTriton shim calls it."""
+    import cutile_b200 as cb
+    from cutile_b200 import TileArray
+
+    M, N, K, E, topk = 200, 256, 192, 5, 2
+    A, B = make(dev, M, N, K, E, 99)
+    ids = routing(M, E, topk, 9)
+    sid, eid, ntp = ops.moe_align(ids.to(dev), E)
+    w = torch.rand(M, topk, generator=torch.Generator().manual_seed(4)).to(dev)
+    C = torch.zeros(M * topk, N, dtype=torch.float16, device=dev)
+    ws = torch.empty(sid.numel() * K, dtype=torch.float16, device=dev)
+    k = cb.triton_kernel("moe", [TileArray(torch.float16, 2), TileArray(torch.float16, 3),
+                                 TileArray(torch.float16, 2)] + [TileArray(torch.int32, 1)] * 3 +
+                         [TileArray(torch.float32, 2), TileArray(torch.float16, 1), int, int])
+    cb.launch(k, 1, A, B, C, sid, eid, ntp, w, ws, topk, 1)
+    torch.cuda.synchronize()
+    ref = O.moe(A.cpu().numpy(), B.cpu().numpy(), sid.cpu().numpy(), eid.cpu().numpy(),
+                int(ntp.item()), topk, w.cpu().numpy())
+    assert O.rel_fro(C.cpu().numpy().astype(np.float64), ref) <= 2e-3
+
+
+def test_transpose_int32_bitwise(dev):
+    x = torch.randint(-2**31, 2**31 - 1, (300, 517), dtype=torch.int32, device=dev)
+    y = torch.empty(517, 300, dtype=torch.int32, device=dev)
+    ops.transpose(x, y)
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), x.cpu().T)
