@@ -16,6 +16,8 @@
 // i overlap the main loop of tile i+1. No cluster multicast anywhere.
 #include "sm100_ptx.cuh"
 
+#include <cstring>
+
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -37,7 +39,12 @@ constexpr int B_STAGE_BYTES = BN * BK * 2;         // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 2 * BN;                  // two accumulators
 constexpr int GROUP_M = 8;                         // L2-friendly tile order
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+// Epilogue staging for TMA stores: per epilogue warp two 32(m) x 32(n) Float16
+// boxes of 2 KB.
+constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
+constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
+constexpr int SMEM_BYTES =
+    STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 constexpr unsigned ERR_BIT = 1u;
 
 struct Params {
@@ -46,6 +53,7 @@ struct Params {
   int64_t ldc, sC;
   int tiles_m, tiles_n, num_kb;
   int64_t num_tiles;
+  int tma_store;  // C written by TMA tensor stores (else 2-byte stores per element)
 };
 
 __device__ __forceinline__ void tile_coords(const Params& p, int64_t t, int& b, int& mt,
@@ -62,15 +70,33 @@ __device__ __forceinline__ void tile_coords(const Params& p, int64_t t, int& b, 
   nt = rr / gsize;
 }
 
+#ifdef CTB_GEMM_TRACE
+// Debug-only timeline (%globaltimer ns) of CTA 0's first tile: 0 start,
+// 1 set-up done, 2 first B/A loads issued, 3 last loads issued, 4 MMA got
+// stage 0, 5 MMA issued the last stage, 6 epilogue got the accumulator,
+// 7 epilogue stored, 8 all roles done, 9 TMEM released.
+__device__ unsigned long long g_gemm_trace[10];
+#define GEMM_TRACE(ev)                                    \
+  do {                                                    \
+    if (blockIdx.x == 0) g_gemm_trace[ev] = global_ns(); \
+  } while (0)
+#else
+#define GEMM_TRACE(ev) \
+  do {                 \
+  } while (0)
+#endif
+
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
-                            const __grid_constant__ CUtensorMap tmB, const Params p) {
+                            const __grid_constant__ CUtensorMap tmB,
+                            const __grid_constant__ CUtensorMap tmC, const Params p) {
   using namespace sm100;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte swizzle atoms need 1024-byte aligned tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;  // [4 warps][2 boxes]
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tmem_full = empty + STAGES;   // [2]
   uint64_t* tmem_empty = tmem_full + 2;   // [2]
@@ -78,6 +104,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) GEMM_TRACE(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -98,6 +125,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) GEMM_TRACE(1);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -116,6 +144,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_3d(sa, &tmA, &full[stage], m0, kb * BK, b);
           tma_load_3d(sa + A_HALF_BYTES, &tmA, &full[stage], m0 + 64, kb * BK, b);
           tma_load_3d(sb, &tmB, &full[stage], kb * BK, n0, b);
+          if (t == blockIdx.x && kb == 0) GEMM_TRACE(2);
+          if (t == blockIdx.x && kb == p.num_kb - 1) GEMM_TRACE(3);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -142,6 +172,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[stage], phase, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
+          if (it == 0 && kb == 0 && lane == 0) GEMM_TRACE(4);
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           // A, MN-major SW128: LBO = 8 KB between the two 64-row halves,
           // SBO = 1 KB between 8-k-row groups; K step of 16 = 2 KB.
@@ -162,46 +193,90 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok) break;
         mma_commit_elect(&tmem_full[buf]);  // accumulator ready for the epilogue
+        if (it == 0 && lane == 0) GEMM_TRACE(5);
       }
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    // TMEM lane m holds row m of the tile. With TMA stores each warp stages
+    // its 32 rows x 32 columns per chunk in shared memory (column-major, as C)
+    // and one lane stores the box; two staging boxes per warp alternate, and
+    // the next chunk's TMEM load is in flight while a chunk is staged.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    __half* stage_w = reinterpret_cast<__half*>(epi_stage + q * 2 * EPI_BOX_BYTES);
+    int sbuf = 0;
     int it = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_bounded(&tmem_full[buf], acc_phase, abort_flag, ERR_BIT)) break;
       tc_fence_after();
+      if (it == 0 && warp == 2 && lane == 0) GEMM_TRACE(6);
       int b, mt, nt;
       tile_coords(p, t, b, mt, nt);
-      const int m = mt * BM + q * 32 + lane;
+      const int m0 = mt * BM + q * 32;
+      const int m = m0 + lane;
       const int n0 = nt * BN;
-      __half* cb = p.C + (int64_t)b * p.sC;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + buf * BN + c + lane_base, r);
-        tmem_ld_wait();
-        if (m < p.M) {
+      const uint32_t tcol = tmem_base + buf * BN + lane_base;
+      if (p.tma_store) {
+        auto stage_chunk = [&](uint32_t (&r)[32], int c) {
+          if (m0 >= p.M || n0 + c >= p.N) return;  // warp-uniform: box wholly outside C
+          __half* sb = stage_w + sbuf * (EPI_BOX_BYTES / 2);
+          if (lane == 0) bulk_wait_read<1>();  // this box's previous store has read it
+          __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + c + j;
-            if (n < p.N) cb[(int64_t)m + (int64_t)n * p.ldc] = __float2half_rn(__uint_as_float(r[j]));
+          for (int j = 0; j < 32; ++j) sb[j * 32 + lane] = __float2half_rn(__uint_as_float(r[j]));
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, sb, m0, n0 + c, b);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        };
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(tcol, ra);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          tmem_ld_wait_regs(ra);
+          tmem_ld_32x32b_x32(tcol + c + 32, rb);
+          stage_chunk(ra, c);
+          tmem_ld_wait_regs(rb);
+          if (c + 64 < BN) tmem_ld_32x32b_x32(tcol + c + 64, ra);
+          stage_chunk(rb, c + 32);
+        }
+      } else {
+        __half* cb = p.C + (int64_t)b * p.sC;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tcol + c, r);
+          tmem_ld_wait_regs(r);
+          if (m < p.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + c + j;
+              if (n < p.N)
+                cb[(int64_t)m + (int64_t)n * p.ldc] = __float2half_rn(__uint_as_float(r[j]));
+            }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&tmem_empty[buf]);
+      if (it == 0 && warp == 2 && lane == 0) GEMM_TRACE(7);
     }
+    if (lane == 0) bulk_wait<0>();  // staged boxes must outlive their stores
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) GEMM_TRACE(8);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+    if (lane == 0) GEMM_TRACE(9);
   }
 }
 
@@ -233,6 +308,41 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
   if (!g_encode) return set_error(CTB_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+#ifndef CTB_NO_TMAP_CACHE
+  // A tensor map is a pure function of these arguments (base address and
+  // geometry, nothing about the memory's contents or lifetime), so a map
+  // encoded once can be reused for any later call with the same arguments.
+  // Small per-thread cache, round-robin replacement, no locking.
+  struct Key {
+    const void* base;
+    uint64_t dims[5], strides[4];
+    uint32_t box[5];
+    int32_t dtype, rank, swizzle, pad;
+  };
+  struct Slot {
+    Key key;
+    CUtensorMap map;
+    bool used;
+  };
+  static thread_local Slot cache[32];
+  static thread_local unsigned next_slot = 0;
+  Key k;
+  std::memset(&k, 0, sizeof(k));
+  k.base = base;
+  k.dtype = (int32_t)dtype;
+  k.rank = rank;
+  k.swizzle = (int32_t)swizzle;
+  for (int i = 0; i < rank && i < 5; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i < rank - 1 && i < 4) k.strides[i] = strides_bytes[i];
+  }
+  for (Slot& sl : cache)
+    if (sl.used && std::memcmp(&sl.key, &k, sizeof(k)) == 0) {
+      *map = sl.map;
+      return CTB_OK;
+    }
+#endif
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = g_encode(map, dtype, (cuuint32_t)rank, const_cast<void*>(base),
                         reinterpret_cast<const cuuint64_t*>(dims),
@@ -243,10 +353,24 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
   if (r != CUDA_SUCCESS)
     return set_error(CTB_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected the operand (CUresult " +
                                          std::to_string((int)r) + ")");
+#ifndef CTB_NO_TMAP_CACHE
+  Slot& sl = cache[next_slot++ % 32];
+  sl.key = k;
+  sl.map = *map;
+  sl.used = true;
+#endif
   return CTB_OK;
 }
 
 int gemm_take_device_error(unsigned int* out) { return take_device_error(out); }
+
+#ifdef CTB_GEMM_TRACE
+extern "C" int ctb_gemm_trace_read(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, gemm::g_gemm_trace, sizeof(gemm::g_gemm_trace)) == cudaSuccess
+             ? 0
+             : -6;
+}
+#endif
 
 static bool g_gemm_attr_done[64];
 static std::mutex g_gemm_mu;
@@ -308,7 +432,21 @@ static int gemm_f16_dispatch(const __half* A, const __half* B, __half* C, int M,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
+  CUtensorMap tmC;
+  const bool c_tma = tma_ok(C, ldc, sC, batch);
+  if (c_tma) {
+    const uint64_t dims[3] = {(uint64_t)M, (uint64_t)N, (uint64_t)batch};
+    const uint64_t strides[2] = {(uint64_t)ldc * 2,
+                                 (uint64_t)(batch > 1 ? sC : ldc * N) * 2};
+    const uint32_t box[3] = {32, 32, 1};
+    if (int rc = encode_tmap(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, C, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  } else {
+    std::memset(&tmC, 0, sizeof(tmC));
+  }
   gemm::Params p;
+  p.tma_store = c_tma ? 1 : 0;
   p.C = C;
   p.M = M;
   p.N = N;
@@ -321,7 +459,7 @@ static int gemm_f16_dispatch(const __half* A, const __half* B, __half* C, int M,
   p.num_kb = (K + gemm::BK - 1) / gemm::BK;
   p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   const int grid = (int)std::min<int64_t>(p.num_tiles, pr.sm_count);
-  gemm::gemm_f16_tcgen05_kernel<<<grid, gemm::THREADS, gemm::SMEM_BYTES, st>>>(tmA, tmB, p);
+  gemm::gemm_f16_tcgen05_kernel<<<grid, gemm::THREADS, gemm::SMEM_BYTES, st>>>(tmA, tmB, tmC, p);
   return launch_status("gemm_f16_tcgen05_kernel");
 }
 
