@@ -25,12 +25,18 @@ namespace ctb {
 // w is read through the read-only path; dW/dB partials stay in registers.
 constexpr unsigned LNBWD_ERR_BIT = 4u;
 
-// Ring depth: two stages where both fit the shared memory of one CTA.
+// Ring depth and CTAs per SM per row-length class. Measured at 16384 x 4096:
+// one CTA per SM with a 4-stage ring (128 KB of x/dy in flight per SM, and
+// half the dW/dB partial rows of two CTAs per SM) is fastest.
+//   n <= 2048  (512 threads, 1 float4):  2 stages x 16 KB, 4 CTAs per SM
+//   n <= 4096  (512 threads, 2 float4):  4 stages x 32 KB, 1 CTA per SM
+//   n <= 8192  (512 threads, 4 float4):  3 stages x 64 KB, 1 CTA per SM
+//   n <= 16384 (1024 threads, 4 float4): 1 stage of 128 KB, 1 CTA per SM
 __host__ __device__ constexpr int lnbwd_stages(int threads, int nv) {
-  return 2 * 2 * threads * nv * 16 <= 160 * 1024 ? 2 : 1;
+  return threads >= 1024 ? 1 : (nv >= 4 ? 3 : (nv >= 2 ? 4 : 2));
 }
 __host__ __device__ constexpr int lnbwd_ctas_per_sm(int threads, int nv) {
-  return threads >= 1024 ? 1 : (nv >= 4 ? 1 : (nv >= 2 ? 2 : 4));
+  return threads >= 1024 ? 1 : (nv >= 2 ? 1 : 4);
 }
 __host__ __device__ constexpr int lnbwd_smem_bytes(int threads, int nv) {
   return lnbwd_stages(threads, nv) * 2 * threads * nv * 16 + 64;

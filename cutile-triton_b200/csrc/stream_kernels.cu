@@ -319,16 +319,23 @@ static int launch_softmax(const float* x, float* y, int len, int count, int64_t 
 // write-back time (32 KB shared by every CTA of the SM, so they hit L1/L2),
 // which keeps registers low and lets more rows be in flight per SM.
 template <int THREADS, int NV, bool VEC>
-__global__ void __launch_bounds__(THREADS, (THREADS >= 1024 ? 1 : 2048 / THREADS)) layernorm_fwd_reg_kernel(
+__global__ void __launch_bounds__(THREADS, (THREADS >= 1024 ? 1 : (NV >= 4 ? 1024 : 1536) / THREADS))
+    layernorm_fwd_reg_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
     float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int n, int rows,
     int64_t ldx, int64_t ldy, float eps) {
   __shared__ float red[THREADS / 32];
   const float inv_n = 1.0f / (float)n;
   const int t = threadIdx.x;
+  // Software pipeline: the next row's loads are issued before this row's
+  // reductions, so two rows per CTA are in flight from HBM.
+  float nv[NV * 4];
+  if (blockIdx.x < rows) load_row<THREADS, NV, VEC>(x + (int64_t)blockIdx.x * ldx, n, 0.f, nv);
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     float v[NV * 4];
-    load_row<THREADS, NV, VEC>(x + row * ldx, n, 0.f, v);
+#pragma unroll
+    for (int i = 0; i < NV * 4; ++i) v[i] = nv[i];
+    if (row + gridDim.x < rows) load_row<THREADS, NV, VEC>(x + (row + gridDim.x) * ldx, n, 0.f, nv);
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < NV * 4; ++i) s += v[i];
