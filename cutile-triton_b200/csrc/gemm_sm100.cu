@@ -16,6 +16,7 @@
 // i overlap the main loop of tile i+1. No cluster multicast anywhere.
 #include "sm100_ptx.cuh"
 
+#include <cstdlib>
 #include <cstring>
 
 #include <cudaTypedefs.h>
@@ -290,6 +291,208 @@ __global__ void zero_cols_kernel(__half* C, int M, int N, int batch, int64_t ldc
   }
 }
 
+
+// -----------------------------------------------------------------------------
+// CTA-pair variant: one 256 x 256 tile per pair of SMs (tcgen05 cta_group::2).
+// Each CTA loads its own 128 rows of A and 128 columns of B per 64-deep
+// k-block (32 KB, against 48 KB per SM for a 128 x 256 tile on one SM: TMA
+// delivers about 78 bytes per clock per SM from L2, and one SM's 128 x 256 x
+// 64 step needs 96 per clock at the full MMA rate). The even CTA issues
+// 256 x 256 x 16 MMAs that read both CTAs' operands; each CTA keeps its 128
+// accumulator rows in its own tensor memory and writes them out itself.
+// Barriers: full[s] lives in the even CTA and counts both CTAs' bytes;
+// empty[s] and tmem_full[b] exist in both CTAs and are arrived by multicast
+// commits; tmem_empty[b] lives in the even CTA and counts all 256 epilogue
+// threads of the pair.
+// -----------------------------------------------------------------------------
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2;  // this CTA's 128 rows of A (two 64-row boxes)
+constexpr int P_B_BYTES = 128 * BK * 2;  // this CTA's 128 columns of B
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + EPI_BYTES + 1024 + 256;
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmC, const Params p) {
+  using namespace sm100;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* epi_stage = smem + P_STAGES * P_STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tmem_full = empty + P_STAGES;  // [2]
+  uint64_t* tmem_empty = tmem_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x / 2, num_pairs = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tmem_full[i], 1);
+      mbar_init(&tmem_empty[i], 256);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised in both CTAs before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full_leader = mapa_shared(smem_u32(&full[0]), 0);
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t t = pair; t < p.num_tiles && !*abort_flag; t += num_pairs) {
+        int b, mt, nt;
+        tile_coords(p, t, b, mt, nt);
+        const int m0 = mt * 256 + (int)rank * 128, n0 = nt * 256 + (int)rank * 128;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, ERR_BIT)) break;
+          uint8_t* sa = smem + stage * P_STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          const uint32_t bar = full_leader + stage * 8;
+          tma_load_3d_pair(sa, &tmA, bar, m0, kb * BK, b);
+          tma_load_3d_pair(sa + A_HALF_BYTES, &tmA, bar, m0 + 64, kb * BK, b);
+          tma_load_3d_pair(sa + P_A_BYTES, &tmB, bar, kb * BK, n0, b);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA only) ----------------
+    if (leader) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, 256, /*a MN-major*/ true, /*b K-major*/ false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < p.num_tiles; t += num_pairs, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tmem_empty[buf], acc_phase ^ 1,
+                                                             abort_flag, ERR_BIT))))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!(ok = __all_sync(0xffffffffu,
+                                mbar_wait_bounded(&full[stage], phase, abort_flag, ERR_BIT))))
+            break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint64_t ad = smem_desc_sw128(sa, A_HALF_BYTES, 1024);
+          const uint64_t bd = smem_desc_sw128(sa + P_A_BYTES, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_ss_pair_elect(d_tmem, ad + (uint64_t)(k * 2048 >> 4),
+                                  bd + (uint64_t)(k * 32 >> 4), idesc, (kb | k) != 0);
+          mma_commit_pair_both_elect(&empty[stage]);  // frees the stage in both CTAs
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair_both_elect(&tmem_full[buf]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    __half* stage_w = reinterpret_cast<__half*>(epi_stage + q * 2 * EPI_BOX_BYTES);
+    const uint32_t tmem_empty_leader = mapa_shared(smem_u32(&tmem_empty[0]), 0);
+    int sbuf = 0;
+    int it = 0;
+    for (int64_t t = pair; t < p.num_tiles && !*abort_flag; t += num_pairs, ++it) {
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_bounded(&tmem_full[buf], acc_phase, abort_flag, ERR_BIT)) break;
+      tc_fence_after();
+      int b, mt, nt;
+      tile_coords(p, t, b, mt, nt);
+      const int m0 = mt * 256 + (int)rank * 128 + q * 32;
+      const int m = m0 + lane;
+      const int n0 = nt * BN;
+      const uint32_t tcol = tmem_base + buf * BN + lane_base;
+      if (p.tma_store) {
+        auto stage_chunk = [&](uint32_t (&r)[32], int c) {
+          if (m0 >= p.M || n0 + c >= p.N) return;
+          __half* sb = stage_w + sbuf * (EPI_BOX_BYTES / 2);
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sb[j * 32 + lane] = __float2half_rn(__uint_as_float(r[j]));
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, sb, m0, n0 + c, b);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        };
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(tcol, ra);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          tmem_ld_wait_regs(ra);
+          tmem_ld_32x32b_x32(tcol + c + 32, rb);
+          stage_chunk(ra, c);
+          tmem_ld_wait_regs(rb);
+          if (c + 64 < BN) tmem_ld_32x32b_x32(tcol + c + 64, ra);
+          stage_chunk(rb, c + 32);
+        }
+      } else {
+        __half* cb = p.C + (int64_t)b * p.sC;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tcol + c, r);
+          tmem_ld_wait_regs(r);
+          if (m < p.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + c + j;
+              if (n < p.N)
+                cb[(int64_t)m + (int64_t)n * p.ldc] = __float2half_rn(__uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      if (leader) mbar_arrive(&tmem_empty[buf]);
+      else mbar_arrive_cluster(tmem_empty_leader + buf * 8);
+    }
+    if (lane == 0) bulk_wait<0>();
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
 }  // namespace gemm
 
 // ---- host --------------------------------------------------------------------
@@ -373,6 +576,7 @@ extern "C" int ctb_gemm_trace_read(unsigned long long* out) {
 #endif
 
 static bool g_gemm_attr_done[64];
+static int g_gemm_pairs[64];
 static std::mutex g_gemm_mu;
 
 int gemm_device_setup() {
@@ -383,8 +587,38 @@ int gemm_device_setup() {
   CTB_CUDA_CHECK(cudaFuncSetAttribute(gemm::gemm_f16_tcgen05_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       gemm::SMEM_BYTES));
-  if (dev < 64) g_gemm_attr_done[dev] = true;
+  CTB_CUDA_CHECK(cudaFuncSetAttribute(gemm::gemm_f16_pair_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      gemm::P_SMEM_BYTES));
+  // Resident CTA pairs (clusters of 2 at one CTA per SM) for the persistent grid.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(gemm::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = gemm::P_SMEM_BYTES;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  CTB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16_pair_kernel, &cfg));
+  if (dev < 64) {
+    g_gemm_pairs[dev] = clusters;
+    g_gemm_attr_done[dev] = true;
+  }
   return CTB_OK;
+}
+
+// Pair kernel choice: CTB_GEMM_PAIR=0 never, =1 whenever possible, unset: when
+// the 256 x 256 tiles fill at least one wave of resident pairs.
+static int gemm_pair_mode() {
+  static const int mode = [] {
+    const char* e = getenv("CTB_GEMM_PAIR");
+    return e ? (e[0] == '1' ? 1 : 0) : -1;
+  }();
+  return mode;
 }
 
 // Tensor-core path eligibility: TMA needs 16-byte aligned bases and strides.
@@ -444,6 +678,47 @@ static int gemm_f16_dispatch(const __half* A, const __half* B, __half* C, int M,
       return rc;
   } else {
     std::memset(&tmC, 0, sizeof(tmC));
+  }
+  int dev = 0;
+  CTB_CUDA_CHECK(cudaGetDevice(&dev));
+  const int pairs = (dev >= 0 && dev < 64) ? g_gemm_pairs[dev] : 0;
+  const int64_t pair_tiles = (int64_t)((M + 255) / 256) * ((N + 255) / 256) * batch;
+  const int mode = gemm_pair_mode();
+  if (pairs > 0 && mode != 0 && (mode == 1 || pair_tiles >= pairs)) {
+    CUtensorMap tmB2;
+    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)batch};
+    const uint64_t strides[2] = {(uint64_t)ldb * 2, (uint64_t)(batch > 1 ? sB : ldb * N) * 2};
+    const uint32_t box[3] = {gemm::BK, 128, 1};
+    if (int rc = encode_tmap(&tmB2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, B, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    gemm::Params pp;
+    pp.tma_store = c_tma ? 1 : 0;
+    pp.C = C;
+    pp.M = M;
+    pp.N = N;
+    pp.K = K;
+    pp.batch = batch;
+    pp.ldc = ldc;
+    pp.sC = sC;
+    pp.tiles_m = (M + 255) / 256;
+    pp.tiles_n = (N + 255) / 256;
+    pp.num_kb = (K + gemm::BK - 1) / gemm::BK;
+    pp.num_tiles = pair_tiles;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(pair_tiles, pairs)), 1, 1);
+    cfg.blockDim = dim3(gemm::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = gemm::P_SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CTB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm::gemm_f16_pair_kernel, tmA, tmB2, tmC, pp));
+    return launch_status("gemm_f16_pair_kernel");
   }
   gemm::Params p;
   p.tma_store = c_tma ? 1 : 0;
