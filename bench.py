@@ -222,14 +222,17 @@ def time_device(case, steps, warmup, dist_on):
     torch.cuda.synchronize()
     per = [s.elapsed_time(e) for s, e in evs]
     total = evs[0][0].elapsed_time(evs[-1][1])
+    srt = sorted(per)
+    stats = [total, sum(per) / len(per), srt[0], srt[len(srt) // 2]]
     if dist_on:
         import torch.distributed as dist
-        t = torch.tensor([total, sum(per) / len(per)], device="cuda")
+        t = torch.tensor(stats, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total, mean = t.tolist()
+        stats = t.tolist()
         dist.barrier()
-        return total, mean
-    return total, sum(per) / len(per)
+    case.launch_stats = {"ms_min": round(stats[2], 5), "ms_median": round(stats[3], 5),
+                         "ms_mean": round(stats[1], 5)}
+    return stats[0], stats[1]
 
 
 def time_e2e(case, steps, dev, dist_on=False):
@@ -543,18 +546,21 @@ def run_reference(args):
     name = args.workload
     desc, unit, _, _ = WORKLOADS[name]
     budget = max(1.0, min(20.0, args.ref_budget))
-    vals = []
+    vals, walls = [], []
     for _ in range(args.warmup):
         cpu_measure(name, 0.2)
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         v, sample, threads = cpu_measure(name, budget / max(1, args.steps))
+        walls.append((time.perf_counter() - t0) * 1e3)
         vals.append(v)
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32" if unit == "GB/s" else "f16 in / f32 acc",
+        "ms_per_step": round(statistics.mean(walls), 3) if walls else None,
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if unit == "GB/s" else "f16",
         "data": "synthetic",
         "config": {"workload": desc, "parallelism": "host threads (rank 0 only)"},
         "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads,
@@ -604,6 +610,7 @@ def run_ours(args):
         res = {"value": round(value, 3), "unit": unit, "ms_per_step": round(total_ms / steps, 5),
                "roofline": roofline(name, mean_ms, peaks, peak_src, traffic),
                "gpu_launches": steps * LAUNCHES_PER_STEP.get(name, 1),
+               "launch_ms": case.launch_stats,
                "dtype": "f16" if bound == "tensor" else "f32",
                "l2": (f"inputs larger than L2 (126 MB): {case.bytes_in() / 1e6:.0f} MB read + "
                       f"{case.bytes_out() / 1e6:.0f} MB written per step")}
@@ -646,6 +653,7 @@ def run_ours(args):
             "config": {"workload": desc, "config_index": 1 if head == "softmax" else None,
                        "parallelism": f"dp{world} (rows; weak scaling, each rank a full config)",
                        "l2": h["l2"]},
+            "launch_ms": h["launch_ms"],
             "roofline": h["roofline"], "cpu_baseline": h.get("cpu_baseline"),
             "e2e": h.get("e2e"), "gpu_launches": h["gpu_launches"], "clocks": clocks,
             "library": cutile_b200.library_path(), "suite": suite, "launch_path": lp,
