@@ -87,6 +87,10 @@ SIGNATURES = {
                       _P],
     "ctb_fmha_fwd_f16": [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P],
     "ctb_moe_workspace_bytes": [_I32, _I32],
+    "ctb_host_workspace_bytes": [_I64, _I64, _I64],
+    "ctb_softmax_f32_host": [_P, _P, _I32, _I32, _P, _I64, _P],
+    "ctb_layernorm_fwd_f32_host": [_P, _P, _P, _P, _P, _P, _I32, _I32, _F, _P, _I64, _P],
+    "ctb_vadd_host": [_I32, _P, _P, _P, _I64, _P, _I64, _P],
     "ctb_moe_gemm_f16": [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                          _I64, _I64, _I64, _P, _I64, _P],
     "ctb_fill_uniform": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
@@ -115,6 +119,7 @@ def load():
         fn.argtypes = args
         fn.restype = ctypes.c_int
     L.ctb_moe_workspace_bytes.restype = ctypes.c_int64
+    L.ctb_host_workspace_bytes.restype = ctypes.c_int64
     L.ctb_last_error.argtypes = []
     L.ctb_last_error.restype = ctypes.c_char_p
     _lib = L

@@ -247,3 +247,66 @@ def moe_gemm(A, B, sorted_ids, expert_ids, ntp, topk, weights=None, out=None, wo
               M, N, K, E, EM, topk, A.stride(0), B.stride(1), out.stride(0),
               ws.data_ptr(), ws.numel() * ws.element_size(), _st())
     return out
+
+
+# ---- host-buffer calls (three-stream chunk pipeline inside the library) -------
+_host_ws = {}
+
+
+def _host_workspace(nbytes, device):
+    key = torch.device(device)
+    ws = _host_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=key)
+        _host_ws[key] = ws
+    return ws
+
+
+def _need_host(*ts):
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.device.type == "cpu" and t.is_contiguous()):
+            raise _lib.B200Error(-1, "expected contiguous host (CPU) tensors")
+
+
+def softmax_host(x, y=None, device=0):
+    """Row softmax of a host (count, len) float32 tensor through the GPU;
+    x and y should be pinned (``pin_memory()``) for the copies to overlap."""
+    _need_host(x)
+    count, length = x.shape
+    y = torch.empty_like(x) if y is None else y
+    L = _lib.load()
+    ws = _host_workspace(L.ctb_host_workspace_bytes(4 * length, 4 * length, count), device)
+    with torch.cuda.device(device):
+        _lib.call("ctb_softmax_f32_host", x.data_ptr(), y.data_ptr(), length, count,
+                  ws.data_ptr(), ws.numel(), _st())
+    return y
+
+
+def layernorm_fwd_host(x, w, b, eps=1e-5, y=None, mean=None, rstd=None, device=0):
+    """LayerNorm over rows of a host (rows, n) float32 tensor through the GPU."""
+    _need_host(x, w, b)
+    rows, n = x.shape
+    y = torch.empty_like(x) if y is None else y
+    mean = torch.empty(rows, dtype=torch.float32) if mean is None else mean
+    rstd = torch.empty(rows, dtype=torch.float32) if rstd is None else rstd
+    L = _lib.load()
+    wb = 2 * ((4 * n + 255) // 256 * 256)
+    ws = _host_workspace(L.ctb_host_workspace_bytes(4 * n, 4 * n + 8, rows) + wb, device)
+    with torch.cuda.device(device):
+        _lib.call("ctb_layernorm_fwd_f32_host", x.data_ptr(), w.data_ptr(), b.data_ptr(),
+                  y.data_ptr(), mean.data_ptr(), rstd.data_ptr(), n, rows, eps, ws.data_ptr(),
+                  ws.numel(), _st())
+    return y, mean, rstd
+
+
+def vadd_host(a, b, c=None, device=0):
+    """c = a + b for host vectors through the GPU."""
+    _need_host(a, b)
+    c = torch.empty_like(a) if c is None else c
+    L = _lib.load()
+    es = a.element_size()
+    ws = _host_workspace(L.ctb_host_workspace_bytes(2 * es, es, a.numel()) + 16 * 256, device)
+    with torch.cuda.device(device):
+        _lib.call("ctb_vadd_host", _DT[a.dtype], a.data_ptr(), b.data_ptr(), c.data_ptr(),
+                  a.numel(), ws.data_ptr(), ws.numel(), _st())
+    return c

@@ -219,6 +219,26 @@ int ctb_fmha_fwd_f16(const void* Q, const void* K, const void* V, void* O,
                      int32_t seq_k, int32_t head_dim, float scale,
                      int32_t causal, void* stream);
 
+/* Host-buffer entry points. The arrays are in host memory (page-locked for
+ * the copies to overlap: cudaHostAlloc or cudaHostRegister); rows (elements
+ * for vadd) move in chunks through `workspace` (device memory, 256-byte
+ * aligned) on three streams of the library so that host-to-device copies, the
+ * kernel and device-to-host copies of successive chunks overlap. The caller's
+ * `stream` first orders the work after what it already holds and is made to
+ * wait for the last copy: the host outputs are complete once `stream` has
+ * completed. Contiguous rows only. Calls on one device enqueue one at a time.
+ * ctb_host_workspace_bytes(in bytes per unit, out bytes per unit, units) is a
+ * workspace size that keeps three chunks of 1/8 of the work in flight;
+ * LayerNorm needs 2 * round_up(4 n, 256) bytes more for w and b. */
+int64_t ctb_host_workspace_bytes(int64_t unit_bytes_in, int64_t unit_bytes_out, int64_t units);
+int ctb_softmax_f32_host(const float* x, float* y, int32_t len, int32_t count, void* workspace,
+                         int64_t workspace_bytes, void* stream);
+int ctb_layernorm_fwd_f32_host(const float* x, const float* w, const float* b, float* y,
+                               float* mean, float* rstd, int32_t n, int32_t rows, float eps,
+                               void* workspace, int64_t workspace_bytes, void* stream);
+int ctb_vadd_host(int32_t dtype, const void* a, const void* b, void* c, int64_t n,
+                  void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Gather-routed mixture-of-experts GEMM (the cuTile moe example is not
  * vendored in the reference; research/bench_final.log:7 benchmarks it). The
  * contract is the published fused-MoE one: `sorted_token_ids` (EM entries,
