@@ -420,7 +420,8 @@ int L_fmha(const ctb_array* x, const double* s, cudaStream_t st) {
 // moe(A, B, C, SORTED, EXPERT_IDS, NTP, WEIGHTS, WORKSPACE, topk, mul_routed_weight):
 // Julia arrays A (K, M), B (K, N, E), C (N, M*topk) Float16 with contiguous
 // first dims (B's experts N*ldb apart); SORTED (EM), EXPERT_IDS (EM/128), NTP
-// (>= 1) Int32; WEIGHTS Float32 (topk, M) contiguous; WORKSPACE Float16
+// (>= 1) Int32 (EM / length(EXPERT_IDS) = 128 or 256 rows per routing block);
+// WEIGHTS Float32 (topk, M) contiguous; WORKSPACE Float16
 // holding at least K*EM elements.
 int L_moe(const ctb_array* x, const double* s, cudaStream_t st) {
   const ctb_array &A = x[0], &B = x[1], &C = x[2], &S = x[3], &EI = x[4], &NT = x[5],
@@ -439,7 +440,8 @@ int L_moe(const ctb_array* x, const double* s, cudaStream_t st) {
   if (mul && W.dtype != CTB_F32) return set_error(CTB_ERR_DTYPE, "moe: weights must be Float32");
   const int K = A.sizes[0], M = A.sizes[1], N = B.sizes[1], E = B.sizes[2], EM = S.sizes[0];
   if (B.sizes[0] != K || C.sizes[0] != N || (int64_t)C.sizes[1] != (int64_t)M * topk ||
-      NT.sizes[0] < 1 || (int64_t)EI.sizes[0] * 128 < EM)
+      NT.sizes[0] < 1 || EI.sizes[0] < 1 ||
+      (EM != (int64_t)EI.sizes[0] * 128 && EM != (int64_t)EI.sizes[0] * 256))
     return set_error(CTB_ERR_SHAPE, "moe: A/B/C/routing sizes disagree");
   if (A.strides[0] != 1 || B.strides[0] != 1 || C.strides[0] != 1 || S.strides[0] != 1 ||
       EI.strides[0] != 1 || (int64_t)B.strides[2] != (int64_t)B.strides[1] * N)
@@ -454,7 +456,8 @@ int L_moe(const ctb_array* x, const double* s, cudaStream_t st) {
   }
   return ctb_moe_gemm_f16(A.ptr, B.ptr, C.ptr, (const int32_t*)S.ptr, (const int32_t*)EI.ptr,
                           (const int32_t*)NT.ptr, mul ? (const float*)W.ptr : nullptr, mul, M,
-                          N, K, E, EM, topk, A.strides[1], B.strides[1], C.strides[1], WS.ptr,
+                          N, K, E, EM, topk, EM == (int64_t)EI.sizes[0] * 256 ? 256 : 128,
+                          A.strides[1], B.strides[1], C.strides[1], WS.ptr,
                           ws_elems * 2, st);
 }
 

@@ -272,6 +272,14 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, ui
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t bar_cluster,
+                                                 int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
 __device__ __forceinline__ void mma_f16_ss_pair_elect(uint32_t d_tmem, uint64_t adesc,
                                                       uint64_t bdesc, uint32_t idesc,
                                                       uint32_t accumulate) {

@@ -92,7 +92,7 @@ SIGNATURES = {
     "ctb_layernorm_fwd_f32_host": [_P, _P, _P, _P, _P, _P, _I32, _I32, _F, _P, _I64, _P],
     "ctb_vadd_host": [_I32, _P, _P, _P, _I64, _P, _I64, _P],
     "ctb_moe_gemm_f16": [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
-                         _I64, _I64, _I64, _P, _I64, _P],
+                         _I32, _I64, _I64, _I64, _P, _I64, _P],
     "ctb_fill_uniform": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
     "ctb_fill_normal": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
 }

@@ -187,7 +187,7 @@ def fmha(q, k, v, scale, causal=False, out=None):
     return out
 
 
-MOE_BLOCK = 128
+MOE_BLOCK = 256  # rows per routing block: 256 runs the CTA-pair kernel, 128 the single-SM one
 
 
 def moe_align(topk_ids, num_experts, block=MOE_BLOCK):
@@ -241,10 +241,11 @@ def moe_gemm(A, B, sorted_ids, expert_ids, ntp, topk, weights=None, out=None, wo
     out = torch.zeros(M * topk, N, dtype=A.dtype, device=A.device) if out is None else out
     w = weights.reshape(-1).contiguous() if weights is not None else None
     ws = moe_workspace(EM, K, A.device) if workspace is None else workspace
+    block_m = EM // max(expert_ids.numel(), 1)
     _lib.call("ctb_moe_gemm_f16", A.data_ptr(), B.data_ptr(), out.data_ptr(),
               sorted_ids.data_ptr(), expert_ids.data_ptr(), ntp.data_ptr(),
               w.data_ptr() if w is not None else None, 1 if w is not None else 0,
-              M, N, K, E, EM, topk, A.stride(0), B.stride(1), out.stride(0),
+              M, N, K, E, EM, topk, block_m, A.stride(0), B.stride(1), out.stride(0),
               ws.data_ptr(), ws.numel() * ws.element_size(), _st())
     return out
 

@@ -258,7 +258,7 @@ int ctb_moe_gemm_f16(const void* A, const void* B, void* C,
                      const int32_t* num_tokens_post_padded,
                      const float* topk_weights, int32_t mul_routed_weight,
                      int32_t M, int32_t N, int32_t K, int32_t E, int32_t EM,
-                     int32_t topk, int64_t lda, int64_t ldb, int64_t ldc,
+                     int32_t topk, int32_t block_m, int64_t lda, int64_t ldb, int64_t ldc,
                      void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---- seeded synthetic inputs (bench / test plumbing, not a cuTile op) ---- */

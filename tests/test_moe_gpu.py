@@ -28,6 +28,7 @@ def make(dev, M, N, K, E, seed):
     return A, B
 
 
+@pytest.mark.parametrize("block", [128, 256])
 @pytest.mark.parametrize("M,N,K,E,topk,weighted,skew", [
     (64, 256, 128, 4, 2, False, False),
     (300, 200, 136, 7, 3, True, False),
@@ -35,53 +36,55 @@ def make(dev, M, N, K, E, seed):
     (5, 64, 8, 3, 1, False, False),
     (2048, 768, 512, 16, 4, True, False),
 ])
-def test_moe_gemm(dev, M, N, K, E, topk, weighted, skew):
+def test_moe_gemm(dev, M, N, K, E, topk, weighted, skew, block):
     A, B = make(dev, M, N, K, E, 21 + M)
     ids = routing(M, E, topk, M, skew)
-    sid, eid, ntp = ops.moe_align(ids.to(dev), E)
+    sid, eid, ntp = ops.moe_align(ids.to(dev), E, block)
     w = torch.rand(M, topk, generator=torch.Generator().manual_seed(3)).to(dev) if weighted else None
     C = ops.moe_gemm(A, B, sid, eid, ntp, topk, w)
     torch.cuda.synchronize()
     ref = O.moe(A.cpu().numpy(), B.cpu().numpy(), sid.cpu().numpy(), eid.cpu().numpy(),
-                int(ntp.item()), topk, None if w is None else w.cpu().numpy())
+                int(ntp.item()), topk, None if w is None else w.cpu().numpy(), block=block)
     got = C.cpu().numpy().astype(np.float64)
     assert O.rel_fro(got, ref) <= 2e-3
     assert np.all(np.isfinite(got))
 
 
-def test_moe_align_matches_oracle_loops(dev):
+@pytest.mark.parametrize("block", [128, 256])
+def test_moe_align_matches_oracle_loops(dev, block):
     ids = routing(333, 9, 3, 5, skew=True)
-    s, e, n = ops.moe_align(ids.to(dev), 9)
-    rs, re, rn = O.moe_align(ids.numpy(), 9)
+    s, e, n = ops.moe_align(ids.to(dev), 9, block)
+    rs, re, rn = O.moe_align(ids.numpy(), 9, block)
     np.testing.assert_array_equal(s.cpu().numpy(), rs)
     np.testing.assert_array_equal(e.cpu().numpy(), re)
     assert int(n.item()) == rn
 
 
-def test_moe_unlisted_rows_and_invalid_blocks_untouched(dev):
+@pytest.mark.parametrize("block", [128, 256])
+def test_moe_unlisted_rows_and_invalid_blocks_untouched(dev, block):
     """Blocks past num_tokens_post_padded and blocks with expert id -1 are
     skipped; the rows they list keep their preset value."""
-    M, N, K, E, topk = 256, 256, 128, 2, 1
+    M, N, K, E, topk = 2 * block, 256, 128, 2, 1
     A, B = make(dev, M, N, K, E, 7)
-    sid = torch.arange(M, dtype=torch.int32, device=dev)            # 2 blocks of 128
+    sid = torch.arange(M, dtype=torch.int32, device=dev)            # 2 blocks
     eid = torch.tensor([-1, 1], dtype=torch.int32, device=dev)
     ntp = torch.tensor([M], dtype=torch.int32, device=dev)
     out = torch.full((M, N), 3.0, dtype=torch.float16, device=dev)
     ops.moe_gemm(A, B, sid, eid, ntp, topk, out=out)
     torch.cuda.synchronize()
     got = out.cpu().numpy().astype(np.float64)
-    assert np.all(got[:128] == 3.0)
-    ref = A.cpu().double()[128:] @ B.cpu().double()[1].T
-    assert O.rel_fro(got[128:], ref.numpy()) <= 2e-3
+    assert np.all(got[:block] == 3.0)
+    ref = A.cpu().double()[block:] @ B.cpu().double()[1].T
+    assert O.rel_fro(got[block:], ref.numpy()) <= 2e-3
     # num_tokens_post_padded below EM: the second block is no longer in use
     out.fill_(3.0)
-    ntp.fill_(128)
+    ntp.fill_(block)
     eid[0] = 0
     ops.moe_gemm(A, B, sid, eid, ntp, topk, out=out)
     torch.cuda.synchronize()
     got = out.cpu().numpy().astype(np.float64)
-    assert np.all(got[128:] == 3.0)
-    assert O.rel_fro(got[:128], (A.cpu().double()[:128] @ B.cpu().double()[0].T).numpy()) <= 2e-3
+    assert np.all(got[block:] == 3.0)
+    assert O.rel_fro(got[:block], (A.cpu().double()[:block] @ B.cpu().double()[0].T).numpy()) <= 2e-3
 
 
 def test_moe_bad_layout_reported(dev):
@@ -113,7 +116,7 @@ def test_moe_through_the_registry(dev):
     cb.launch(k, 1, A, B, C, sid, eid, ntp, w, ws, topk, 1)
     torch.cuda.synchronize()
     ref = O.moe(A.cpu().numpy(), B.cpu().numpy(), sid.cpu().numpy(), eid.cpu().numpy(),
-                int(ntp.item()), topk, w.cpu().numpy())
+                int(ntp.item()), topk, w.cpu().numpy(), block=sid.numel() // eid.numel())
     assert O.rel_fro(C.cpu().numpy().astype(np.float64), ref) <= 2e-3
 
 

@@ -8,15 +8,16 @@ from oracle import oracle as O
 
 
 def test_moe_align_cpu_matches_loops():
-    for M, E, topk, seed in [(1, 4, 1, 0), (100, 8, 2, 1), (333, 9, 3, 2), (7, 64, 4, 3)]:
+    for (M, E, topk, seed), block in zip([(1, 4, 1, 0), (100, 8, 2, 1), (333, 9, 3, 2), (7, 64, 4, 3)],
+                                         [128, 256, 128, 256]):
         g = torch.Generator().manual_seed(seed)
         ids = torch.argsort(torch.rand(M, E, generator=g), dim=1)[:, :topk].to(torch.int32)
-        s, e, n = ops.moe_align(ids, E)
-        rs, re, rn = O.moe_align(ids.numpy(), E)
+        s, e, n = ops.moe_align(ids, E, block)
+        rs, re, rn = O.moe_align(ids.numpy(), E, block)
         np.testing.assert_array_equal(s.numpy(), rs)
         np.testing.assert_array_equal(e.numpy(), re)
         assert int(n.item()) == rn
-        assert s.numel() % 128 == 0 and e.numel() * 128 == s.numel()
+        assert s.numel() % block == 0 and e.numel() * block == s.numel()
 
 
 def test_moe_oracle_against_dense():
