@@ -22,7 +22,7 @@
 // running max is only moved when it grows by more than 8 (a factor 256), so
 // the O rescale in TMEM is rare; numerator and denominator always share the
 // same max, so the result is unchanged.
-// No cluster multicast anywhere; every wait is bounded.
+// Every TMA load fills one CTA's own shared memory; every wait is bounded.
 #include "sm100_ptx.cuh"
 
 #include <algorithm>

@@ -13,7 +13,7 @@
 //   warp 1      TMEM owner + MMA issuer (one elected thread)
 //   warps 2..5  epilogue: tcgen05.ld -> f16 -> global
 // Two 256-column accumulators in TMEM (512 columns) let the epilogue of tile
-// i overlap the main loop of tile i+1. No cluster multicast anywhere.
+// i overlap the main loop of tile i+1. Every TMA load fills one CTA's own shared memory.
 #include "sm100_ptx.cuh"
 
 #include <cstdlib>
@@ -301,8 +301,8 @@ __global__ void zero_cols_kernel(__half* C, int M, int N, int batch, int64_t ldc
 // 256 x 256 x 16 MMAs that read both CTAs' operands; each CTA keeps its 128
 // accumulator rows in its own tensor memory and writes them out itself.
 // Barriers: full[s] lives in the even CTA and counts both CTAs' bytes;
-// empty[s] and tmem_full[b] exist in both CTAs and are arrived by multicast
-// commits; tmem_empty[b] lives in the even CTA and counts all 256 epilogue
+// empty[s] and tmem_full[b] exist in both CTAs and are arrived by commits to
+// both CTAs; tmem_empty[b] lives in the even CTA and counts all 256 epilogue
 // threads of the pair.
 // -----------------------------------------------------------------------------
 constexpr int P_STAGES = 6;

@@ -21,7 +21,7 @@
 // (2) The GEMM's persistent 128 x 256 x 64 tcgen05 pipeline on A_perm: one
 // producer thread loads A_perm's 128 x 64 box and the expert's 256 x 64 B
 // slab by TMA per stage; the epilogue thread of TMEM lane r scatters row r of
-// the tile to C[s] with 16-byte stores. No cluster multicast; every wait is
+// the tile to C[s] with 16-byte stores. Every TMA load fills one CTA's own shared memory; every wait is
 // bounded.
 #include "sm100_ptx.cuh"
 
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // A_perm and 128 columns of the expert's B by TMA (32 KB per k-block, counted
 // on the even CTA's full barrier), keeps its 128 accumulator rows in its own
 // tensor memory and scatters them itself. Same barrier protocol as the pair
-// GEMM: multicast commits free stages and publish accumulators in both CTAs,
+// GEMM: commits to both CTAs free stages and publish accumulators,
 // both CTAs' epilogue threads arrive on the even CTA's accumulator-empty
 // barrier, cluster barriers at start and end.
 constexpr int P_STAGES = 6;

@@ -263,7 +263,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 }
 // 3-D tiled load into this CTA's shared memory whose completion is counted on
 // an mbarrier of either CTA of the pair (`bar_cluster` is a shared::cluster
-// address). No multicast.
+// address). Each load fills only this CTA's shared memory.
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, uint32_t bar_cluster,
                                                  int c0, int c1, int c2) {
   asm volatile(
@@ -292,14 +292,19 @@ __device__ __forceinline__ void mma_f16_ss_pair_elect(uint32_t d_tmem, uint64_t 
       : "memory");
 }
 // Arrive once on `bar` (same shared-memory offset) in both CTAs of the pair
-// when this thread's previously issued pair MMAs finish.
+// when this thread's previously issued pair MMAs finish: one commit to this
+// CTA's barrier and one to the peer's (its shared::cluster address); both
+// track the same MMAs. Issued by the even CTA, so the peer is rank 1.
 __device__ __forceinline__ void mma_commit_pair_both_elect(uint64_t* bar) {
+  const uint32_t local = smem_u32(bar);
+  const uint32_t peer = mapa_shared(local, 1);
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
-      "h"((uint16_t)3)
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%1];\n\t}" ::"r"(
+          local),
+      "r"(peer)
       : "memory");
 }
 
