@@ -24,7 +24,8 @@ using CUDA
 using Libdl
 import cuTile as ct
 
-export triton_kernel, triton_kernel_candidates, launch!, install_shim!, use_b200!, B200Kernel
+export triton_kernel, triton_kernel_candidates, launch!, install_shim!, use_b200!, B200Kernel,
+       softmax_host!, layernorm_fwd_host!, vadd_host!, moe_align
 
 # ---------------------------------------------------------------------------- library
 const LIBPATH = Ref{String}("")
@@ -231,6 +232,81 @@ function install_shim!()
         return $(TileTritonB200).get_kernel(f, tt)
     end
     return nothing
+end
+
+# ---- host-buffer calls: arrays in (pinned) host memory, chunks pipelined through
+# a device workspace on the library's streams; synchronise the stream to read results.
+const HOST_WS = Ref{Any}(nothing)
+function host_workspace(nbytes::Integer)
+    ws = HOST_WS[]
+    if ws === nothing || sizeof(ws) < nbytes
+        ws = CuArray{UInt8}(undef, max(Int(nbytes), 256))
+        HOST_WS[] = ws
+    end
+    return ws
+end
+wsbytes(inb, outb, units) = ccall(sym(:ctb_host_workspace_bytes), Int64, (Int64, Int64, Int64),
+                                  inb, outb, units)
+
+"y = softmax over each column of the host matrix x (len x count), through the GPU."
+function softmax_host!(y::Matrix{Float32}, x::Matrix{Float32})
+    len, count = size(x)
+    ws = host_workspace(wsbytes(4len, 4len, count))
+    check(ccall(sym(:ctb_softmax_f32_host), Cint,
+                (Ptr{Float32}, Ptr{Float32}, Int32, Int32, CuPtr{UInt8}, Int64, Ptr{Cvoid}),
+                x, y, len, count, ws, sizeof(ws), CUDA.stream().handle))
+    CUDA.synchronize()
+    return y
+end
+
+"LayerNorm over each column of the host matrix x (n x rows): y, mean, rstd on the host."
+function layernorm_fwd_host!(y::Matrix{Float32}, mean::Vector{Float32}, rstd::Vector{Float32},
+                             x::Matrix{Float32}, w::Vector{Float32}, b::Vector{Float32}, eps=1f-5)
+    n, rows = size(x)
+    ws = host_workspace(wsbytes(4n, 4n + 8, rows) + 2 * cld(4n, 256) * 256)
+    check(ccall(sym(:ctb_layernorm_fwd_f32_host), Cint,
+                (Ptr{Float32}, Ptr{Float32}, Ptr{Float32}, Ptr{Float32}, Ptr{Float32}, Ptr{Float32},
+                 Int32, Int32, Float32, CuPtr{UInt8}, Int64, Ptr{Cvoid}),
+                x, w, b, y, mean, rstd, n, rows, eps, ws, sizeof(ws), CUDA.stream().handle))
+    CUDA.synchronize()
+    return y, mean, rstd
+end
+
+"c = a + b for host vectors, through the GPU."
+function vadd_host!(c::Vector{T}, a::Vector{T}, b::Vector{T}) where {T<:Union{Float16,Float32,Float64}}
+    ws = host_workspace(wsbytes(2sizeof(T), sizeof(T), length(a)) + 16 * 256)
+    check(ccall(sym(:ctb_vadd_host), Cint,
+                (Int32, Ptr{T}, Ptr{T}, Ptr{T}, Int64, CuPtr{UInt8}, Int64, Ptr{Cvoid}),
+                dtype_code(T), a, b, c, length(a), ws, sizeof(ws), CUDA.stream().handle))
+    CUDA.synchronize()
+    return c
+end
+
+"""
+    moe_align(topk_ids::Matrix{<:Integer}, num_experts; block=256)
+
+Fused-MoE routing for the `moe` kernel from a (topk, tokens) matrix of
+0-based expert ids: (sorted_token_ids, expert_ids, num_tokens_post_padded) as
+Int32 vectors, slots grouped by expert in slot order, each expert padded to a
+multiple of `block` (256: CTA-pair kernel, 128: single-SM kernel) with the id
+tokens*topk. Move them to the device with `CuArray`.
+"""
+function moe_align(topk_ids::AbstractMatrix{<:Integer}, num_experts::Integer; block::Integer=256)
+    flat = vec(topk_ids)  # slot s = token * topk + choice (column-major (topk, tokens))
+    n = length(flat)
+    sorted = Int32[]
+    experts = Int32[]
+    for e in 0:num_experts-1
+        slots = [Int32(s - 1) for s in 1:n if flat[s] == e]
+        pad = mod(-length(slots), block)
+        append!(sorted, slots, fill(Int32(n), pad))
+        append!(experts, fill(Int32(e), (length(slots) + pad) ÷ block))
+    end
+    if isempty(sorted)
+        sorted = fill(Int32(n), block)
+        experts = Int32[-1]
+    end
+    return sorted, experts, Int32[length(sorted)]
 end
 
 "Initialises the library on the active CUDA device (kernel attributes, checks sm_100)."
