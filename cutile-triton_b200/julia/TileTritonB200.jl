@@ -302,11 +302,12 @@ function moe_align(topk_ids::AbstractMatrix{<:Integer}, num_experts::Integer; bl
         append!(sorted, slots, fill(Int32(n), pad))
         append!(experts, fill(Int32(e), (length(slots) + pad) ÷ block))
     end
-    if isempty(sorted)
+    em = length(sorted)
+    if em == 0  # nothing routed: one padding block with no expert, none in use
         sorted = fill(Int32(n), block)
         experts = Int32[-1]
     end
-    return sorted, experts, Int32[length(sorted)]
+    return sorted, experts, Int32[em]
 end
 
 "Initialises the library on the active CUDA device (kernel attributes, checks sm_100)."
