@@ -95,3 +95,23 @@ def test_python_error_carries_status():
     with pytest.raises(cutile_b200.B200Error) as e:
         cutile_b200.triton_kernel("fft", [cutile_b200.TileArray(__import__("torch").float32, 1)])
     assert e.value.status == "CTB_ERR_UNKNOWN_KERNEL"
+
+
+def test_new_entry_points_validate_without_gpu():
+    L = _lib.load()
+    # MoE: routing block must be 128 or 256, EM a multiple of it; checked before any device call.
+    args = [None] * 7 + [0, 16, 64, 64, 2, 256, 1]
+    assert L.ctb_moe_gemm_f16(*args, 64, 64, 64, 64, None, 0, None) == -3
+    assert L.ctb_moe_gemm_f16(*args[:12], 384, 1, 256, 64, 64, 64, None, 0, None) == -3
+    assert b"multiple of block_m" in L.ctb_last_error()
+    assert L.ctb_moe_workspace_bytes(256, 64) == 256 * 64 * 2
+    # Host-buffer calls: NULL pointers and bad sizes are reported, empty work is a no-op.
+    assert L.ctb_softmax_f32_host(None, None, 16, 4, None, 0, None) == -1
+    assert L.ctb_softmax_f32_host(None, None, -1, 4, None, 0, None) == -3
+    assert L.ctb_softmax_f32_host(None, None, 16, 0, None, 0, None) == 0
+    assert L.ctb_vadd_host(99, None, None, None, 8, None, 0, None) == -2
+    assert L.ctb_layernorm_fwd_f32_host(None, None, None, None, None, None, 0, 4,
+                                        ctypes.c_float(1e-5), None, 0, None) == -3
+    ws = L.ctb_host_workspace_bytes(4 * 16384, 4 * 16384, 4096)
+    assert ws >= 3 * (4096 // 8) * 8 * 16384  # three slots of 1/8 of the rows
+    assert L.ctb_host_workspace_bytes(4, 4, 0) == 0
