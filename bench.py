@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 kernel backend for TileTriton's seven cuTile kernels.
+"""Benchmark of the B200 kernel backend for TileTriton's cuTile kernels.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME] [--no-suite]

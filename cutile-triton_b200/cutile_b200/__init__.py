@@ -3,7 +3,7 @@
 * :mod:`cutile_b200.runtime` mirrors ``TritonRun`` (triton_kernel, launch,
   flatten_args, set_target) over the C ABI of libcutile_b200.so;
 * :mod:`cutile_b200.shim` mirrors ``TritonShim`` (install_shim, get_kernel);
-* :mod:`cutile_b200.ops` holds typed torch-facing calls of the seven kernels.
+* :mod:`cutile_b200.ops` holds typed torch-facing calls of the kernels.
 """
 from . import _lib
 from ._lib import B200Error

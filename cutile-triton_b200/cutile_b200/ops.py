@@ -1,4 +1,4 @@
-"""Typed torch-facing calls of the seven kernels (the C ABI's typed entry
+"""Typed torch-facing calls of the kernels (the C ABI's typed entry
 points). Every call runs on the current torch CUDA stream and raises
 :class:`B200Error` on failure; there is no CPU or eager fallback.
 

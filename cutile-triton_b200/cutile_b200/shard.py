@@ -1,4 +1,4 @@
-"""Data-parallel partition of the seven workloads over ranks (one process
+"""Data-parallel partition of the workloads over ranks (one process
 per GPU). Every unit is independent — vadd elements, rowsum/softmax/
 layernorm rows, GEMM row blocks, batched-GEMM batches, attention
 (batch, head) pairs — so ranks exchange nothing on the data path.

@@ -1,7 +1,7 @@
 """B200 twin of TileTriton's ``TritonShim`` (reference: src/shim.jl).
 
 ``install_shim(ct)`` overrides ``ct.cufunction`` so that every cuTile launch
-of one of the seven kernels goes to the prebuilt sm_100a library, exactly as
+of one of the registered kernels goes to the prebuilt sm_100a library, exactly as
 the reference's ``install_shim!`` (shim.jl:126-131) routes them to Triton.
 ``get_kernel`` keeps the reference cache key ``(f, tt, world)`` (shim.jl:20-36)
 and raises for a kernel the library does not have. The call operator takes

@@ -12,7 +12,7 @@ include/cutile_b200.h.
 - `launch!(k, grid, args...)` flattens exactly like `TritonRun.flatten_args`
   (runtime.jl:163-198) into `ctb_array`s and launches on CUDA.jl's stream.
 - `install_shim!()` overwrites `cuTile.cufunction` so `ct.launch` /
-  `@cuda backend=cuTile` of the seven kernels run here (shim.jl:126-131).
+  `@cuda backend=cuTile` of the registered kernels run here (shim.jl:126-131).
 - `use_b200!()` selects this backend for `TileTriton.triton_kernel` /
   `launch!` callers (see INTEGRATION.md for the two-line hook in TileTriton).
 
@@ -224,7 +224,7 @@ end
 """
     install_shim!()
 
-Route cuTile compilation of the seven kernels to libcutile_b200.so by
+Route cuTile compilation of the registered kernels to libcutile_b200.so by
 overwriting `cuTile.cufunction` (opt-in, like the reference's shim).
 """
 function install_shim!()

@@ -1,14 +1,16 @@
 /*
  * cutile_b200.h — C ABI of libcutile_b200.so, the sm_100a kernel backend that
- * replaces TileTriton's TTIR -> Triton -> cubin pipeline for seven cuTile
- * kernels: vadd, rowsum, softmax, layernorm-fwd, matmul, batchmatmul, fmha.
+ * replaces TileTriton's TTIR -> Triton -> cubin pipeline for the cuTile
+ * kernels vadd, rowsum, softmax, layernorm-fwd, matmul, batchmatmul, fmha,
+ * and the next ones: layernorm backward, transpose, moe.
  *
  * Every entry point:
  *   - takes plain pointers, sizes and strides (no Julia, torch or CUDA types;
  *     `stream` is a cudaStream_t / CUstream passed as void*, NULL = legacy
  *     default stream of the current device);
  *   - works on caller-owned device memory and allocates nothing on the launch
- *     path;
+ *     path (the *_host entry points take host pointers plus a device
+ *     workspace);
  *   - returns CTB_OK (0) or a negative ctb_status and never aborts; the
  *     message of the last failure on the calling thread is ctb_last_error().
  *

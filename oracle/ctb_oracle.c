@@ -1,5 +1,5 @@
 /*
- * ctb_oracle.c — CPU restatement of the seven cuTile kernels TileTriton runs
+ * ctb_oracle.c — CPU restatement of the cuTile kernels TileTriton runs
  * on its hot path. TEST INFRASTRUCTURE ONLY: the parity tests, the smoke
  * check and bench.py's CPU-baseline leg load it as the checker / the timed
  * CPU stand-in; the product library never calls it.

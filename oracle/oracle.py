@@ -1,4 +1,4 @@
-"""CPU oracle for the seven cuTile kernels — TEST INFRASTRUCTURE ONLY.
+"""CPU oracle for the cuTile kernels of the B200 backend — TEST INFRASTRUCTURE ONLY.
 
 Used by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
 --impl reference legs as the checker and the timed CPU stand-in. Nothing in
