@@ -204,19 +204,15 @@ function get_kernel(@nospecialize(f), @nospecialize(tt))
     return k
 end
 
+# Ghost arguments (Constant and other singletons) carry no bytes; dropping them
+# with a recursive tuple filter is specialised per signature, with no Any[].
+drop_ghosts() = ()
+drop_ghosts(a, rest...) = Base.issingletontype(typeof(a)) ? drop_ghosts(rest...) :
+                          (a, drop_ghosts(rest...)...)
+
 # cuTile calls the kernel with converted arguments (TileArrays, ghosts, primitives).
 function (k::B200ShimKernel)(args...; blocks=1, threads=1, convert=Val(false), kwargs...)
-    flat = Any[]
-    for a in args
-        if a isa ct.TileArray
-            push!(flat, a)
-        elseif Base.issingletontype(typeof(a))
-            # ghost (Constant etc.)
-        else
-            push!(flat, a)
-        end
-    end
-    arrays, scalars = flatten_args(k.kernel.argspec, flat)
+    arrays, scalars = flatten_args(k.kernel.argspec, drop_ghosts(args...))
     GC.@preserve args raw_launch(k.kernel.handle, arrays, scalars, normgrid(blocks))
     return nothing
 end
