@@ -652,6 +652,32 @@ def run_ours(args):
             suite[name] = measure(name, steps, max(3, args.warmup), True,
                                   True, args.cpu_budget / 3)
             suite[name]["config"] = WORKLOADS[name][0]
+    gather = None
+    if args.gather and dist_on:
+        # Optional final gather of every rank's headline output (NCCL over
+        # NVLink/NVSwitch), after and apart from the timed kernels.
+        import torch.distributed as dist
+        from cutile_b200.shard import gather_shards
+
+        gcase = Case(head, dev, rank)
+        gcase.run()
+        out = gcase.outputs[0]
+        gather_shards(out)  # warm-up (communicator buffers)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        full = gather_shards(out)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nbytes = out.numel() * out.element_size()
+        gather = {"what": f"all-gather of each rank's {head} output", "bytes_per_rank": nbytes,
+                  "bytes_total": full.numel() * full.element_size(), "ms": round(t.item(), 4),
+                  "GB/s_received_per_rank": round(nbytes * (world - 1) / (t.item() * 1e-3) / 1e9, 1)}
+        del full, gcase
+        torch.cuda.empty_cache()
     lp = launch_path(dev) if (args.suite and rank == 0) else None
     if rank == 0:
         sampler.stop()
@@ -669,6 +695,7 @@ def run_ours(args):
             "roofline": h["roofline"], "cpu_baseline": h.get("cpu_baseline"),
             "e2e": h.get("e2e"), "gpu_launches": h["gpu_launches"], "clocks": clocks,
             "library": cutile_b200.library_path(), "suite": suite, "launch_path": lp,
+            **({"gather": gather} if gather else {}),
         }
         print(json.dumps(line), flush=True)
     if dist_on:
@@ -711,6 +738,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU work for the headline cpu_baseline")
     ap.add_argument("--ref-budget", type=float, default=15.0)
+    ap.add_argument("--gather", action="store_true",
+                    help="under torchrun: also time an all-gather of the headline output (NCCL)")
     ap.add_argument("--full-size", action="store_true",
                     help="with --profile: the bench's own sizes instead of the small case")
     ap.add_argument("--profile", default=None, choices=list(WORKLOADS),

@@ -21,3 +21,17 @@ def weak_offset(units_per_rank, rank):
     job, so per-GPU work stays fixed as N grows; used as the seed counter
     offset so every rank's synthetic inputs are distinct and reproducible."""
     return units_per_rank * rank
+
+
+def gather_shards(local, group=None):
+    """Optional final gather: every rank's equal-sized shard (dim 0) of a
+    result, concatenated in rank order on every rank. Not part of the data
+    path; over NCCL it moves the shards across NVLink/NVSwitch, over gloo
+    it runs on host tensors (used by the CPU tests)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(parts, local.contiguous(), group=group)
+    return torch.cat(parts, dim=0)

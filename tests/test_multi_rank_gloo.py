@@ -62,3 +62,24 @@ def test_shard_range_partitions():
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
     assert shard_range(4096, 1, 8, align=128) == (512, 1024)
     assert weak_offset(4096 * 16384, 3) == 3 * 4096 * 16384
+
+
+def _gather_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from cutile_b200.shard import gather_shards
+
+    local = torch.arange(6, dtype=torch.float32).reshape(3, 2) + 100 * rank
+    full = gather_shards(local)
+    if rank == 1:
+        q.put(full.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gather_shards_concatenates_in_rank_order():
+    q = mp.get_context("spawn").SimpleQueue()
+    mp.spawn(_gather_worker, args=(2, _free_port(), q), nprocs=2, join=True)
+    full = q.get()
+    expect = np.concatenate([np.arange(6, dtype=np.float32).reshape(3, 2) + 100 * r for r in range(2)])
+    np.testing.assert_array_equal(full, expect)
