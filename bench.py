@@ -555,6 +555,15 @@ def run_reference(args):
     from oracle import oracle as O
 
     O.build()
+    # torchrun sets OMP_NUM_THREADS=1 for its ranks; the CPU reference uses every
+    # host thread this process may run on (OpenMP in the C port, the BLAS pool for numpy).
+    ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    O.set_threads(ncpu)
+    try:
+        from threadpoolctl import threadpool_limits
+        blas_limit = threadpool_limits(limits=ncpu)
+    except Exception:  # threadpoolctl absent: BLAS keeps its own default
+        blas_limit = None
     name = args.workload
     desc, unit, _, _ = WORKLOADS[name]
     budget = max(1.0, min(20.0, args.ref_budget))
@@ -567,6 +576,8 @@ def run_reference(args):
         walls.append((time.perf_counter() - t0) * 1e3)
         vals.append(v)
     value = statistics.median(vals)
+    if blas_limit is not None:
+        blas_limit.restore_original_limits()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
