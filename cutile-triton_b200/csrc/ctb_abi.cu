@@ -129,6 +129,7 @@ int fmha_device_setup();
 int gemm_take_device_error(unsigned int* out);
 int fmha_take_device_error(unsigned int* out);
 int moe_take_device_error(unsigned int* out);
+int layernorm_bwd_take_device_error(unsigned int* out);
 }
 
 extern "C" int ctb_init(int device) {
@@ -156,7 +157,10 @@ extern "C" int ctb_check_device(void* stream) {
   if (int e = fmha_take_device_error(&hf)) return cuda_fail((cudaError_t)e, "reading the FMHA error word");
   unsigned int hm = 0;
   if (int e = moe_take_device_error(&hm)) return cuda_fail((cudaError_t)e, "reading the MoE error word");
-  const unsigned int h = hg | hf | hm;
+  unsigned int hl = 0;
+  if (int e = layernorm_bwd_take_device_error(&hl))
+    return cuda_fail((cudaError_t)e, "reading the layernorm backward error word");
+  const unsigned int h = hg | hf | hm | hl;
   if (h) {
     return set_error(CTB_ERR_TIMEOUT, "a bounded device-side wait gave up (error word " +
                                           std::to_string(h) + ")");

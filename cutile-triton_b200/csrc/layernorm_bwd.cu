@@ -198,6 +198,8 @@ __global__ void __launch_bounds__(32 * FOLD_SLICES) layernorm_bwd_dwdb_kernel(
   }
 }
 
+int layernorm_bwd_take_device_error(unsigned int* out) { return take_device_error(out); }
+
 int layernorm_bwd_groups(int n, int rows, int sm_count) {
   if (n <= 0 || rows <= 0) return 1;
   const int per_sm = n <= 2048 ? lnbwd_ctas_per_sm(512, 1)
