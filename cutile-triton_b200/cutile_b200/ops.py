@@ -255,6 +255,8 @@ _host_ws = {}
 
 
 def _host_workspace(nbytes, device):
+    """One workspace per device for the host-buffer calls; they run on the
+    current stream, which orders successive calls that share it."""
     key = torch.device(device)
     ws = _host_ws.get(key)
     if ws is None or ws.numel() < nbytes:

@@ -228,7 +228,9 @@ int ctb_fmha_fwd_f16(const void* Q, const void* K, const void* V, void* O,
  * kernel and device-to-host copies of successive chunks overlap. The caller's
  * `stream` first orders the work after what it already holds and is made to
  * wait for the last copy: the host outputs are complete once `stream` has
- * completed. Contiguous rows only. Calls on one device enqueue one at a time.
+ * completed. Contiguous rows only. Calls on one device enqueue one at a time;
+ * calls that share a workspace must also be ordered on the device (the same
+ * `stream`, or synchronised in between), since each call reuses its slots.
  * ctb_host_workspace_bytes(in bytes per unit, out bytes per unit, units) is a
  * workspace size that keeps three chunks of 1/8 of the work in flight;
  * LayerNorm needs 2 * round_up(4 n, 256) bytes more for w and b. */
