@@ -26,6 +26,7 @@
 #include "sm100_ptx.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace ctb {
@@ -54,15 +55,16 @@ struct Params {
   int mul;
   int M, N, K, E, EM, topk;
   int64_t lda, ldc;
-  int tiles_n, num_kb, num_mblk;
+  int tiles_n, num_kb, num_mblk;  // num_mblk: tiles of tile_rows rows in sorted order
   int group_m;  // m-blocks per raster group
-  int bm;       // rows per routing block: 128 (one SM per tile) or 256 (a CTA pair)
+  int bm;         // rows per routing block (128 or 256): one expert per block
+  int tile_rows;  // rows per output tile: 128 (one SM) or 256 (a CTA pair, bm == 256)
 };
 
 // Blocks in use: those below num_tokens_post_padded.
 __device__ __forceinline__ int blocks_in_use(const Params& p) {
   const int ntp = __ldg(p.ntp);
-  return max(min(p.num_mblk, (ntp + p.bm - 1) / p.bm), 0);
+  return max(min(p.num_mblk, (ntp + p.tile_rows - 1) / p.tile_rows), 0);
 }
 
 // Raster order: groups of group_m consecutive m-blocks (about one expert's
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int64_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int mb, n0;
         tile_coords(p, mblk, t, mb, n0);
-        int e = __ldg(p.expert_ids + mb);
+        int e = __ldg(p.expert_ids + (int64_t)mb * p.tile_rows / p.bm);
         if (e < 0 || e >= p.E) e = p.E;  // out of range: the TMA fills zeros
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, ERR_BIT)) break;
@@ -188,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int mb, n0;
       tile_coords(p, mblk, t, mb, n0);
       const int sid = __ldg(p.sorted + (int64_t)mb * BM + r);
-      const int e = __ldg(p.expert_ids + mb);
+      const int e = __ldg(p.expert_ids + (int64_t)mb * p.tile_rows / p.bm);
       const bool valid = sid >= 0 && sid < p.M * p.topk && e >= 0 && e < p.E;
       const float wt = (valid && p.mul) ? __ldg(p.w + sid) : 1.f;
       __half* crow = p.C + (int64_t)(valid ? sid : 0) * p.ldc;
@@ -296,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int64_t t = pair; t < num_tiles && !*abort_flag; t += num_pairs) {
         int mb, n0;
         tile_coords(p, mblk, t, mb, n0);
-        int e = __ldg(p.expert_ids + mb);
+        int e = __ldg(p.expert_ids + (int64_t)mb * p.tile_rows / p.bm);
         if (e < 0 || e >= p.E) e = p.E;  // out of range: the TMA fills zeros
         const int row0 = mb * 256 + (int)rank * 128, col0 = n0 + (int)rank * 128;
         for (int kb = 0; kb < p.num_kb; ++kb) {
@@ -365,7 +367,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int mb, n0;
       tile_coords(p, mblk, t, mb, n0);
       const int sid = __ldg(p.sorted + (int64_t)mb * 256 + r);
-      const int e = __ldg(p.expert_ids + mb);
+      const int e = __ldg(p.expert_ids + (int64_t)mb * p.tile_rows / p.bm);
       const bool valid = sid >= 0 && sid < p.M * p.topk && e >= 0 && e < p.E;
       const float wt = (valid && p.mul) ? __ldg(p.w + sid) : 1.f;
       __half* crow = p.C + (int64_t)(valid ? sid : 0) * p.ldc;
@@ -415,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 __global__ void __launch_bounds__(128) moe_gather_rows_kernel(const Params p, __half* Ap,
                                                                int64_t ldp) {
   const int i = blockIdx.x;
-  if (i >= blocks_in_use(p) * p.bm) return;
+  if (i >= blocks_in_use(p) * p.tile_rows) return;
   const int sid = __ldg(p.sorted + i);
   if (sid < 0 || sid >= p.M * p.topk) return;
   const uint4* src = reinterpret_cast<const uint4*>(p.A + (int64_t)(sid / p.topk) * p.lda);
@@ -530,21 +532,31 @@ extern "C" int ctb_moe_gemm_f16(const void* A, const void* B, void* C,
   p.ldc = ldc;
   p.tiles_n = (N + moe::BN - 1) / moe::BN;
   p.num_kb = (K + moe::BK - 1) / moe::BK;
+  // 256-row blocks run on CTA pairs unless CTB_MOE_PAIR=0 or no pair can be
+  // resident; the single-SM kernel serves any block size (per 128-row tile).
+  int pairs = 0;
+  {
+    int dev = 0;
+    CTB_CUDA_CHECK(cudaGetDevice(&dev));
+    pairs = (dev >= 0 && dev < 64) ? g_moe_pairs[dev] : 0;
+  }
+  static const bool pair_off = [] {
+    const char* e = getenv("CTB_MOE_PAIR");
+    return e && e[0] == '0';
+  }();
+  const bool use_pair = block_m == 256 && pairs > 0 && !pair_off;
   p.bm = block_m;
-  p.num_mblk = EM / block_m;
+  p.tile_rows = use_pair ? 256 : 128;
+  p.num_mblk = EM / p.tile_rows;
   // Raster groups of about 4096 routed rows (32 blocks of 128 measured best of
   // 1..300 blocks on the 8-expert top-2 workload; the same rows for 256-row blocks).
-  p.group_m = std::max(1, CTB_MOE_GROUP_ROWS / block_m);
+  p.group_m = std::max(1, CTB_MOE_GROUP_ROWS / p.tile_rows);
   const int64_t max_tiles = (int64_t)p.num_mblk * p.tiles_n;
   const int grid = (int)std::min<int64_t>(max_tiles, pr.sm_count);
   moe::moe_gather_rows_kernel<<<EM, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       p, (__half*)workspace, K);
   if (int rc = launch_status("moe_gather_rows_kernel")) return rc;
-  if (block_m == 256) {
-    int dev = 0;
-    CTB_CUDA_CHECK(cudaGetDevice(&dev));
-    const int pairs = (dev >= 0 && dev < 64) ? g_moe_pairs[dev] : 0;
-    if (pairs < 1) return set_error(CTB_ERR_CUDA, "moe: no resident CTA pair for the 256-row kernel");
+  if (use_pair) {
     CUtensorMap tmB2;
     const uint32_t box2[3] = {moe::BK, 128, 1};
     if (int rc = encode_tmap(&tmB2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, B, dims, strides, box2,

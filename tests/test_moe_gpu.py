@@ -126,3 +126,38 @@ def test_transpose_int32_bitwise(dev):
     ops.transpose(x, y)
     torch.cuda.synchronize()
     assert torch.equal(y.cpu(), x.cpu().T)
+
+
+def test_moe_256_row_blocks_on_the_single_sm_kernel():
+    """256-row routing blocks also run on the single-SM kernel (the fallback
+    when no CTA pair can be resident), forced with CTB_MOE_PAIR=0 in a child."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = r"""
+import json, sys
+sys.path.insert(0, "cutile-triton_b200"); sys.path.insert(0, ".")
+import numpy as np, torch
+from cutile_b200 import ops
+from oracle import oracle as O
+dev = torch.device("cuda", 0)
+A = ops.fill_uniform(torch.empty(700, 136, dtype=torch.float16, device=dev), 1)
+B = ops.fill_uniform(torch.empty(5, 296, 136, dtype=torch.float16, device=dev), 2)
+g = torch.Generator().manual_seed(3)
+ids = torch.argsort(torch.rand(700, 5, generator=g), dim=1)[:, :2].to(torch.int32).to(dev)
+w = torch.rand(700, 2, generator=g).to(dev)
+sid, eid, ntp = ops.moe_align(ids, 5, 256)
+C = ops.moe_gemm(A, B, sid, eid, ntp, 2, w)
+torch.cuda.synchronize(); ops.check_device()
+ref = O.moe(A.cpu().numpy(), B.cpu().numpy(), sid.cpu().numpy(), eid.cpu().numpy(),
+            int(ntp.item()), 2, w.cpu().numpy(), block=256)
+print(json.dumps(O.rel_fro(C.cpu().numpy().astype(np.float64), ref)))
+"""
+    env = dict(os.environ, CTB_MOE_PAIR="0")
+    r = subprocess.run([sys.executable, "-c", script], cwd=root, env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert json.loads(r.stdout.strip().splitlines()[-1]) <= 2e-3
