@@ -7,6 +7,9 @@ copied into this repository):
     by TileTriton's own emitter for the cuTile `vadd` (tile 1024) and
     `rowsum` (tile 64 x 128, TMA descriptors) kernels of test/runtests.jl;
     compiled with the recipe of bench/compile_ttir.py:16-19.
+  * research/matmul_emitted.ttir — TileTriton's TTIR for the tf32 `matmul`
+    kernel of test/runtests.jl:70-84 (128 x 128 x 32 tiles, 8 warps as that
+    test launches it, device-built TMA descriptors).
   * bench/bench_compile.py:45-57 — the Python-Triton twin of the persistent
     column softmax, compiled with TILE = 1024 (the test/runtests.jl:120 case).
 
@@ -49,6 +52,10 @@ def main():
         src = os.path.join(REF, "research", f"{name}_emitted.ttir")
         k = tt_compile(src, target=target, options={"num_warps": 4, "num_stages": 3})
         print(name, _write(f"{name}_ttir", k))
+
+    src = os.path.join(REF, "research", "matmul_emitted.ttir")
+    k = tt_compile(src, target=target, options={"num_warps": 8, "num_stages": 3})
+    print("matmul", _write("matmul_ttir", k))
 
     # Python-twin softmax: take the function definition from the reference
     # file's syntax tree (the module itself writes files on import).

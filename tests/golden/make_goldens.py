@@ -11,7 +11,11 @@ bits tests regenerate on the host), and writes:
   ref_goldens.json  sha256 of every full output + metadata
   ref_goldens.npz   rowsum outputs and sampled softmax columns
 
-Usage (on a machine with a B200):  python tests/golden/make_goldens.py [OUT_DIR]
+With `matmul` as the first argument it instead runs the reference's tf32
+matmul TTIR (test/runtests.jl:70-98 shapes, grid (cld(M,128), cld(N,128)))
+and writes ref_goldens_matmul.json / .npz (full outputs).
+
+Usage (on a machine with a B200):  python tests/golden/make_goldens.py [matmul] [OUT_DIR]
 (OUT_DIR defaults to tests/golden/).
 """
 import ctypes
@@ -33,6 +37,7 @@ VADD_CASES = [(1_024_000, 1, 2), (999_999, 1, 2), (1 << 28, 20261201, 20261202)]
 ROWSUM_CASES = [(4096, 128, 3), (131072, 128, 5)]
 SOFTMAX_CASE = (1000, 2048, 4, 512)  # n_rows, n_cols, seed, grid
 SOFTMAX_COLS = list(range(8)) + list(range(8, 2048, 256))
+MATMUL_CASES = [(512, 512, 512, 31, 32), (300, 260, 200, 33, 34)]  # test/runtests.jl:86
 
 
 def sha(a):
@@ -64,7 +69,13 @@ def main():
         _, fn, md = k
         ptrs = (ctypes.c_void_p * len(args))(*[ctypes.addressof(a) for a in args])
         st = torch.cuda.current_stream().cuda_stream
-        (err,) = cu.cuLaunchKernel(fn, grid, 1, 1, md["num_warps"] * 32, 1, 1, md["shared"], st,
+        gx, gy = grid if isinstance(grid, tuple) else (grid, 1)
+        if md["shared"] > 48 * 1024:
+            (err,) = cu.cuFuncSetAttribute(
+                fn, cu.CUfunction_attribute.CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                md["shared"])
+            assert err == cu.CUresult.CUDA_SUCCESS, err
+        (err,) = cu.cuLaunchKernel(fn, gx, gy, 1, md["num_warps"] * 32, 1, 1, md["shared"], st,
                                    ctypes.addressof(ptrs), 0)
         assert err == cu.CUresult.CUDA_SUCCESS, err
         torch.cuda.synchronize()
@@ -72,6 +83,36 @@ def main():
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     I = ctypes.c_int32  # noqa: E741
     NULL = ctypes.c_void_p(0)
+    if len(sys.argv) > 1 and sys.argv[1] == "matmul":
+        k = load("matmul_ttir")
+        gss, gsa = k[2]["global_scratch_size"], k[2]["global_scratch_align"]
+        mout = {"generator": "SplitMix64 counter stream, oracle.uniform(lo=0, hi=1)",
+                "kernel": "research/matmul_emitted.ttir (tf32, 128x128x32, 8 warps)",
+                "cases": []}
+        marrays = {}
+        for M, N, K, sa, sb in MATMUL_CASES:
+            A_jl = O.uniform(M * K, sa, lo=0.0, hi=1.0).reshape(K, M)  # Julia M x K, stride (1, M)
+            B_jl = O.uniform(K * N, sb, lo=0.0, hi=1.0).reshape(N, K)  # Julia K x N, stride (1, K)
+            A, B = torch.from_numpy(A_jl).to(dev), torch.from_numpy(B_jl).to(dev)
+            C = torch.zeros(N, M, device=dev)  # Julia M x N
+            grid = ((M + 127) // 128, (N + 127) // 128)
+            scratch = torch.zeros(grid[0] * grid[1] * gss + gsa, dtype=torch.uint8, device=dev)
+            sp = ctypes.c_void_p((scratch.data_ptr() + gsa - 1) // gsa * gsa)
+            launch(k, grid, [P(A), I(M), I(K), I(1), I(M), P(B), I(K), I(N), I(1), I(K),
+                             P(C), I(M), I(N), I(1), I(M), sp, NULL])
+            hc = C.cpu().numpy()
+            mout["cases"].append({"M": M, "N": N, "K": K, "seed_a": sa, "seed_b": sb,
+                                  "sha256": sha(hc)})
+            marrays[f"matmul_{M}x{N}x{K}"] = hc
+            print("matmul", M, N, K, sha(hc)[:16])
+        dst = sys.argv[2] if len(sys.argv) > 2 else HERE
+        os.makedirs(dst, exist_ok=True)
+        with open(os.path.join(dst, "ref_goldens_matmul.json"), "w") as f:
+            json.dump(mout, f, indent=1)
+        np.savez_compressed(os.path.join(dst, "ref_goldens_matmul.npz"), **marrays)
+        print("written", os.path.join(dst, "ref_goldens_matmul.json"))
+        return 0
+
     out = {"generator": "SplitMix64 counter stream, oracle.uniform (see oracle/ctb_oracle.c)",
            "kernels": "reference TTIR / Python-Triton twins compiled by oracle/build_ref.py",
            "vadd": [], "rowsum": [], "softmax": {}}

@@ -44,3 +44,30 @@ def test_oracle_softmax_matches_reference_kernel():
     cols = c["sampled_columns"]
     got = O.softmax(x_jl[cols])
     assert O.isapprox(got, A["softmax_sampled"], 1e-5)
+
+
+GM = json.load(open(os.path.join(HERE, "ref_goldens_matmul.json")))
+AM = np.load(os.path.join(HERE, "ref_goldens_matmul.npz"))
+
+
+def _matmul_inputs(case):
+    M, N, K = case["M"], case["N"], case["K"]
+    A = O.uniform(M * K, case["seed_a"], lo=0.0, hi=1.0).reshape(K, M)  # Julia M x K
+    B = O.uniform(K * N, case["seed_b"], lo=0.0, hi=1.0).reshape(N, K)  # Julia K x N
+    return A, B
+
+
+@pytest.mark.parametrize("case", GM["cases"], ids=lambda c: f"{c['M']}x{c['N']}x{c['K']}")
+def test_oracle_matmul_matches_reference_tf32_kernel(case):
+    """The float64 GEMM restatement against the reference's own tf32 matmul
+    kernel (research/matmul_emitted.ttir), with test/runtests.jl:95-98's
+    metric and tolerance."""
+    M, N, K = case["M"], case["N"], case["K"]
+    A, B = _matmul_inputs(case)
+    ref = O.matmul(A, B)  # (N, M) = Julia C^T storage
+    if M == 512:
+        cols = GM["sampled"]["512x512x512"]["julia_columns_n"]
+        got, ref = AM["matmul_512x512x512_cols"], ref[cols]
+    else:
+        got = AM[f"matmul_{M}x{N}x{K}"]
+    assert O.max_rel(got, ref) < 1e-3

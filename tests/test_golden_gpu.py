@@ -50,3 +50,37 @@ def test_softmax_matches_reference_kernel(dev):
     torch.cuda.synchronize()
     got = y.cpu().numpy()[c["sampled_columns"]]
     assert O.isapprox(got, A["softmax_sampled"], 1e-5)
+
+
+GM = json.load(open(os.path.join(HERE, "ref_goldens_matmul.json")))
+AM = np.load(os.path.join(HERE, "ref_goldens_matmul.npz"))
+
+
+@pytest.mark.parametrize("case", GM["cases"], ids=lambda c: f"{c['M']}x{c['N']}x{c['K']}")
+def test_float32_matmul_matches_reference_tf32_kernel(dev, case):
+    """Our Float32 matmul (registry `matmul`, the reference test's launch) on the
+    inputs the reference's tf32 kernel saw, against that kernel's output with
+    test/runtests.jl:95-98's metric and tolerance."""
+    import cutile_b200 as cb
+    from cutile_b200 import Constant, TileArray
+
+    def matmul(A, B, C, tm, tn, tk):
+        pass
+
+    M, N, K = case["M"], case["N"], case["K"]
+    A = torch.empty(K, M, device=dev)
+    B = torch.empty(N, K, device=dev)
+    ops.fill_uniform(A, case["seed_a"], 0.0, 1.0)
+    ops.fill_uniform(B, case["seed_b"], 0.0, 1.0)
+    C = torch.zeros(N, M, device=dev)
+    k = cb.triton_kernel(matmul, [TileArray(torch.float32, 2)] * 3 +
+                         [Constant(128), Constant(128), Constant(32)])
+    cb.launch(k, ((M + 127) // 128, (N + 127) // 128), A, B, C)
+    torch.cuda.synchronize()
+    got = C.cpu().numpy()
+    if M == 512:
+        cols = GM["sampled"]["512x512x512"]["julia_columns_n"]
+        got, ref = got[cols], AM["matmul_512x512x512_cols"]
+    else:
+        ref = AM[f"matmul_{M}x{N}x{K}"]
+    assert O.max_rel(got, ref) < 1e-3
