@@ -1,7 +1,9 @@
-// CUDA-core attention forward: one warp per query row, online softmax over
-// key chunks of 32. It serves head dims and sequence shapes the tensor-core
-// kernel does not take, and is the independent on-device cross-check of
-// that kernel in the tests. Same contract as ctb_fmha_fwd_f16.
+// CUDA-core attention forward (the cuTile example fmha.jl:20, not vendored in
+// the reference; report.html:2981 describes its 4-D head-dim-contiguous tiles):
+// one warp per query row, online softmax over key chunks of 32. It serves head
+// dims and sequence shapes the tensor-core kernel does not take, and is the
+// independent on-device cross-check of that kernel in the tests. Same contract
+// as ctb_fmha_fwd_f16.
 #include "ctb_common.cuh"
 
 namespace ctb {

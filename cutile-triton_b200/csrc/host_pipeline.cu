@@ -4,7 +4,10 @@
 // copies, kernels, device-to-host copies — so that, in steady state, chunk
 // i+1 is copied in while chunk i is computed and chunk i-1 is copied out.
 // PCIe moves data both ways at once, so a row-wise kernel fed from host memory
-// runs at the one-way copy rate instead of half of it.
+// runs at the one-way copy rate instead of half of it. They replace the round
+// trip a Julia caller writes around a launch — device arrays filled from host
+// data, `launch!`, `Array(c)` back (the pattern of test/runtests.jl:42-46) —
+// with one call.
 //
 // Ordering with the caller: the copy stream first waits for everything
 // already enqueued on the caller's stream, and the caller's stream is made to
