@@ -39,7 +39,10 @@ constexpr int A_STAGE_BYTES = BM * BK * 2;         // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;         // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 2 * BN;                  // two accumulators
-constexpr int GROUP_M = 8;                         // L2-friendly tile order
+#ifndef CTB_GEMM_GROUP_M
+#define CTB_GEMM_GROUP_M 8
+#endif
+constexpr int GROUP_M = CTB_GEMM_GROUP_M;          // L2-friendly tile order (m-tiles per group)
 // Epilogue staging for TMA stores: per epilogue warp two 32(m) x 32(n) Float16
 // boxes of 2 KB.
 constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
