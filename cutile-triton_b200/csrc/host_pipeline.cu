@@ -24,8 +24,14 @@
 namespace ctb {
 namespace {
 
-constexpr int NSLOT = 3;           // chunks in flight through the workspace
-constexpr int MIN_CHUNKS = 8;      // split work at least this finely when it is large
+#ifndef CTB_HOST_SLOTS
+#define CTB_HOST_SLOTS 3
+#endif
+#ifndef CTB_HOST_CHUNKS
+#define CTB_HOST_CHUNKS 8
+#endif
+constexpr int NSLOT = CTB_HOST_SLOTS;        // chunks in flight through the workspace
+constexpr int MIN_CHUNKS = CTB_HOST_CHUNKS;  // split work at least this finely when it is large
 constexpr int64_t MIN_CHUNK_BYTES = 4 << 20;
 constexpr int MAX_ARRAYS = 3;
 
