@@ -49,6 +49,10 @@ constexpr int TILE_BYTES = BQ * D * 2;       // 32 KB: one 128 x 128 f16 tile
 constexpr int HALF_BYTES = TILE_BYTES / 2;   // one 64-wide (128-byte) TMA box
 constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
+#ifndef CTB_FMHA_P_PARTS
+#define CTB_FMHA_P_PARTS 2
+#endif
+constexpr int P_PARTS = CTB_FMHA_P_PARTS;     // P published in this many key ranges per block
 constexpr unsigned ERR_BIT = 2u;
 
 struct Params {
@@ -164,13 +168,14 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
 // columns 0-63; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
 // 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
 __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j,
-                                         int half) {
+                                         int part) {
   using namespace sm100;
   constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
+  constexpr int STEPS = BKV / 16 / P_PARTS;  // 16-key MMA steps per published part
   const uint32_t va = sVa + stage * TILE_BYTES;
 #pragma unroll
-  for (int k4 = 0; k4 < BKV / 32; ++k4) {
-    const int kk = half * (BKV / 32) + k4;
+  for (int k4 = 0; k4 < STEPS; ++k4) {
+    const int kk = part * STEPS + k4;
     mma_f16_ts_elect(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
                      smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
                      (j > 0 || kk > 0) ? 1u : 0u);
@@ -195,7 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* p_full = bars + 20;  // [2 tiles][2 halves of the keys]
+  uint64_t* p_full = bars + 20;  // [2 tiles][P_PARTS key ranges]
   uint64_t* o_full = bars + 13;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 #ifdef CTB_FMHA_TRACE
@@ -220,8 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[2 * i], SM_THREADS_PER_TILE);
-      mbar_init(&p_full[2 * i + 1], SM_THREADS_PER_TILE);
+      for (int q = 0; q < P_PARTS; ++q) mbar_init(&p_full[P_PARTS * i + q], SM_THREADS_PER_TILE);
       mbar_init(&o_full[i], 1);
 #ifdef CTB_FMHA_TRACE
       mbar_init(&grp_done[2 * i], 1);
@@ -288,12 +292,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT)))) break;
         if (lane == 0) FMHA_TRACE(8, j);
         // P*V on the first 64 keys starts while the softmax finishes the rest.
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[0], j & 1, abort_flag, ERR_BIT)))) break;
-        tc_fence_after();
-        issue_pv(tmem, sVa, 0, s, j, 0);
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[1], j & 1, abort_flag, ERR_BIT)))) break;
-        tc_fence_after();
-        issue_pv(tmem, sVa, 0, s, j, 1);
+        for (int q = 0; q < P_PARTS && ok; ++q) {
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[q], j & 1, abort_flag, ERR_BIT)))) break;
+          tc_fence_after();
+          issue_pv(tmem, sVa, 0, s, j, q);
+        }
+        if (!ok) break;
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[0]);
 #endif
@@ -307,12 +311,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
           if (lane == 0) FMHA_TRACE(6, j);
         }
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[2], j & 1, abort_flag, ERR_BIT)))) break;
-        tc_fence_after();
-        issue_pv(tmem, sVa, 1, s, j, 0);
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[3], j & 1, abort_flag, ERR_BIT)))) break;
-        tc_fence_after();
-        issue_pv(tmem, sVa, 1, s, j, 1);
+        for (int q = 0; q < P_PARTS && ok; ++q) {
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[P_PARTS + q], j & 1, abort_flag, ERR_BIT)))) break;
+          tc_fence_after();
+          issue_pv(tmem, sVa, 1, s, j, q);
+        }
+        if (!ok) break;
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[2]);
 #endif
@@ -434,10 +438,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           pk[i] = pack_half2(ea, eb);
         }
         tmem_st_32x32b_x16(s_col + c * 16, pk);
-        if (c & 1) {
+        if ((c + 1) % (4 / P_PARTS) == 0) {
           tmem_st_wait();
           tc_fence_before();
-          mbar_arrive(&p_full[t * 2 + (c >> 1)]);
+          mbar_arrive(&p_full[t * P_PARTS + c / (4 / P_PARTS)]);
         }
       }
       float s0, s1, s2, s3;
