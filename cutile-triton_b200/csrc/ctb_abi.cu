@@ -130,6 +130,7 @@ int gemm_take_device_error(unsigned int* out);
 int fmha_take_device_error(unsigned int* out);
 int moe_take_device_error(unsigned int* out);
 int layernorm_bwd_take_device_error(unsigned int* out);
+int selftest_take_device_error(unsigned int* out);
 }
 
 extern "C" int ctb_init(int device) {
@@ -160,7 +161,10 @@ extern "C" int ctb_check_device(void* stream) {
   unsigned int hl = 0;
   if (int e = layernorm_bwd_take_device_error(&hl))
     return cuda_fail((cudaError_t)e, "reading the layernorm backward error word");
-  const unsigned int h = hg | hf | hm | hl;
+  unsigned int hs = 0;
+  if (int e = selftest_take_device_error(&hs))
+    return cuda_fail((cudaError_t)e, "reading the self-test error word");
+  const unsigned int h = hg | hf | hm | hl | hs;
   if (h) {
     return set_error(CTB_ERR_TIMEOUT, "a bounded device-side wait gave up (error word " +
                                           std::to_string(h) + ")");

@@ -42,7 +42,8 @@ int current_props(DeviceProps* out);
 
 // ---- device error word ------------------------------------------------------
 // Set by a kernel whose bounded wait gave up; read by ctb_check_device.
-// Codes: bit 0 = GEMM pipeline wait, bit 1 = FMHA pipeline wait.
+// Bits: 1 = GEMM, 2 = FMHA, 4 = LayerNorm backward, 8 = MoE pipeline wait,
+// 32 = the wait self-test (ctb_selftest_wait_timeout).
 // The library is built without relocatable device code, so every translation
 // unit owns its copy; a unit whose kernels flag errors exposes a reader
 // (take_device_error) that ctb_check_device polls.

@@ -71,9 +71,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 #ifndef CTB_WAIT_SUSPEND_NS
 #define CTB_WAIT_SUSPEND_NS 20000u
 #endif
+// Default limit of every pipeline wait, in ns (build-time: -DCTB_WAIT_LIMIT_NS=...).
+#ifndef CTB_WAIT_LIMIT_NS
+#define CTB_WAIT_LIMIT_NS 4000000000ull
+#endif
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag, unsigned err_bit,
-                                                  uint64_t limit_ns = 4000000000ull) {
+                                                  uint64_t limit_ns = CTB_WAIT_LIMIT_NS) {
   if (mbar_try_wait_sleep(bar, parity, CTB_WAIT_SUSPEND_NS)) return true;
   const uint64_t t0 = global_ns();
   while (true) {

@@ -95,6 +95,7 @@ SIGNATURES = {
                          _I32, _I64, _I64, _I64, _P, _I64, _P],
     "ctb_fill_uniform": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
     "ctb_fill_normal": [_P, _I32, _I64, _U64, _U64, _D, _D, _P],
+    "ctb_selftest_wait_timeout": [_I64, _P, _P],
 }
 
 _lib = None

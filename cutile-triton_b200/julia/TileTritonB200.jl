@@ -14,7 +14,8 @@ include/cutile_b200.h.
 - `install_shim!()` overwrites `cuTile.cufunction` so `ct.launch` /
   `@cuda backend=cuTile` of the registered kernels run here (shim.jl:126-131).
 - `use_b200!()` selects this backend for `TileTriton.triton_kernel` /
-  `launch!` callers (see INTEGRATION.md for the two-line hook in TileTriton).
+  `launch!` callers (TileTriton's own `triton_kernel`/`launch!` forward here
+  when the active target's backend is "b200").
 
 The library path is `ENV["CUTILE_B200_LIB"]`, else the in-tree build.
 """

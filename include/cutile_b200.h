@@ -276,6 +276,20 @@ int ctb_fill_uniform(void* ptr, int32_t dtype, int64_t n, uint64_t seed,
 int ctb_fill_normal(void* ptr, int32_t dtype, int64_t n, uint64_t seed,
                     uint64_t offset, double mean, double std, void* stream);
 
+/* ---- failure-path self-test (test plumbing, not a cuTile op) ------------- */
+
+/* Launches one CTA whose warp 0 holds 32 TMEM columns and waits on an
+ * mbarrier that nothing arrives on, giving up after `limit_ns` (1..1e9);
+ * its warp 1 waits on the same barrier with the library's default limit
+ * and leaves through the CTA abort flag. The TMEM is released before the
+ * CTA returns. `status` (device memory, 3 ints): [0] = 1 when warp 0's wait
+ * gave up, [1] = 1 when warp 1's did, [2] = the ns warp 1 waited. The next
+ * ctb_check_device returns CTB_ERR_TIMEOUT and clears the error word; the
+ * context stays usable. It exercises the exit path that every pipeline wait
+ * of this library takes (the reference reports no device-side timeouts:
+ * its kernels have no bounded waits). */
+int ctb_selftest_wait_timeout(int64_t limit_ns, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

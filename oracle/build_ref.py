@@ -11,11 +11,13 @@ copied into this repository):
     kernel of test/runtests.jl:70-84 (128 x 128 x 32 tiles, 8 warps as that
     test launches it, device-built TMA descriptors).
   * bench/bench_compile.py:45-57 — the Python-Triton twin of the persistent
-    column softmax, compiled with TILE = 1024 (the test/runtests.jl:120 case).
+    column softmax, compiled with TILE = 1024 (the test/runtests.jl:120 case)
+    and with TILE = 16384 (the BASELINE 4096 x 16384 config).
 
 The installed triton is 3.6.0; the reference pins 3.7.1 (CondaPkg.toml:8),
 which is not installable offline. Outputs: <name>.cubin + <name>.json
-(launch metadata). Run here (needs the reference tree); the GPU box only
+(launch metadata). Usage: python oracle/build_ref.py <reference tree>
+(or $CTB_REFERENCE_ROOT). Run here (needs the reference tree); the GPU box only
 loads the results.
 """
 import ast
@@ -23,7 +25,8 @@ import json
 import os
 import sys
 
-REF = os.environ.get("CTB_REFERENCE_ROOT", "/root/reference")
+# The reference tree: first argument, else $CTB_REFERENCE_ROOT (no default).
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CTB_REFERENCE_ROOT", "")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref")
 
 
@@ -74,6 +77,14 @@ def main():
                     constexprs={"TILE": 1024})
     k = tt_compile(src, target=target, options={"num_warps": 4, "num_stages": 3})
     print("softmax_py", _write("softmax_py", k))
+    # The BASELINE config (4096 vectors of 16384): TILE = 16384, one column per
+    # tile as the cuTile example runs it; 16 warps keep the tile in registers.
+    src = ASTSource(fn=ns["softmax"],
+                    signature={"out": "*fp32", "inp": "*fp32", "n_rows": "i32", "n_cols": "i32",
+                               "stride_o": "i32", "stride_i": "i32", "TILE": "constexpr"},
+                    constexprs={"TILE": 16384})
+    k = tt_compile(src, target=target, options={"num_warps": 16, "num_stages": 3})
+    print("softmax_py_16384", _write("softmax_py_16384", k))
     return 0
 
 

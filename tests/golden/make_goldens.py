@@ -15,7 +15,15 @@ With `matmul` as the first argument it instead runs the reference's tf32
 matmul TTIR (test/runtests.jl:70-98 shapes, grid (cld(M,128), cld(N,128)))
 and writes ref_goldens_matmul.json / .npz (full outputs).
 
-Usage (on a machine with a B200):  python tests/golden/make_goldens.py [matmul] [OUT_DIR]
+With `softmax_baseline` it runs the reference's softmax twin compiled with
+TILE = 16384 on the BASELINE config (4096 vectors of 16384 Float32, entries
+4*N(0,1) from oracle.normal, seed 20261201) and writes
+ref_goldens_softmax_baseline.json / .npz: the sha256 of the full output,
+per-vector checksums (max, sum and index-weighted sum, in float64) of all
+4096 vectors, and 4 sampled vectors in full.
+
+Usage (on a machine with a B200):
+    python tests/golden/make_goldens.py [matmul | softmax_baseline] [OUT_DIR]
 (OUT_DIR defaults to tests/golden/).
 """
 import ctypes
@@ -37,6 +45,18 @@ VADD_CASES = [(1_024_000, 1, 2), (999_999, 1, 2), (1 << 28, 20261201, 20261202)]
 ROWSUM_CASES = [(4096, 128, 3), (131072, 128, 5)]
 SOFTMAX_CASE = (1000, 2048, 4, 512)  # n_rows, n_cols, seed, grid
 SOFTMAX_COLS = list(range(8)) + list(range(8, 2048, 256))
+SOFTMAX_BASELINE = (16384, 4096, 20261201, 1184)  # length, count, seed, grid (8 x 148)
+SOFTMAX_BASELINE_VECS = [0, 1, 2047, 4095]
+
+
+def softmax_vector_stats(y):
+    """Per-vector (max, sum, index-weighted sum) of a (count, length) softmax
+    output in float64: a checksum of every vector, compared with the rtol."""
+    y64 = y.astype(np.float64)
+    idx = np.arange(1, y.shape[1] + 1, dtype=np.float64) / y.shape[1]
+    return np.stack([y64.max(axis=1), y64.sum(axis=1), y64 @ idx], axis=1)
+
+
 MATMUL_CASES = [(512, 512, 512, 31, 32), (300, 260, 200, 33, 34)]  # test/runtests.jl:86
 
 
@@ -83,6 +103,27 @@ def main():
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     I = ctypes.c_int32  # noqa: E741
     NULL = ctypes.c_void_p(0)
+    if len(sys.argv) > 1 and sys.argv[1] == "softmax_baseline":
+        k = load("softmax_py_16384")
+        length, count, seed, grid = SOFTMAX_BASELINE
+        xh = O.normal(length * count, seed, 0.0, 4.0).reshape(count, length)
+        x = torch.from_numpy(xh).to(dev)
+        y = torch.zeros_like(x)
+        launch(k, grid, [P(y), P(x), I(length), I(count), I(length), I(length), NULL, NULL])
+        hy = y.cpu().numpy()
+        st = softmax_vector_stats(hy)
+        res = {"kernel": "bench/bench_compile.py:45-57 softmax, TILE 16384, 16 warps",
+               "length": length, "count": count, "seed": seed, "mean": 0.0, "std": 4.0,
+               "generator": "oracle.normal (SplitMix64 + Box-Muller)", "grid": grid,
+               "sha256_input": sha(xh), "sha256": sha(hy), "sampled_vectors": SOFTMAX_BASELINE_VECS}
+        dst = sys.argv[2] if len(sys.argv) > 2 else HERE
+        os.makedirs(dst, exist_ok=True)
+        with open(os.path.join(dst, "ref_goldens_softmax_baseline.json"), "w") as f:
+            json.dump(res, f, indent=1)
+        np.savez_compressed(os.path.join(dst, "ref_goldens_softmax_baseline.npz"), stats=st,
+                            vectors=hy[SOFTMAX_BASELINE_VECS])
+        print("softmax baseline", sha(hy)[:16])
+        return 0
     if len(sys.argv) > 1 and sys.argv[1] == "matmul":
         k = load("matmul_ttir")
         gss, gsa = k[2]["global_scratch_size"], k[2]["global_scratch_align"]

@@ -84,3 +84,37 @@ def test_float32_matmul_matches_reference_tf32_kernel(dev, case):
     else:
         ref = AM[f"matmul_{M}x{N}x{K}"]
     assert O.max_rel(got, ref) < 1e-3
+
+
+_SB = os.path.join(HERE, "ref_goldens_softmax_baseline.json")
+
+
+@pytest.mark.slow
+@pytest.mark.skipif(not os.path.exists(_SB), reason="BASELINE-size softmax golden not generated")
+def test_softmax_baseline_config_matches_reference_kernel(dev):
+    """The headline config (4096 vectors of 16384 Float32, 4*N(0,1)) against
+    the reference's own softmax kernel compiled with TILE = 16384: every
+    vector's checksums and four whole vectors within rtol 1e-5."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("make_goldens",
+                                                  os.path.join(HERE, "make_goldens.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    softmax_vector_stats = mg.softmax_vector_stats
+    c = json.load(open(_SB))
+    g = np.load(_SB.replace(".json", ".npz"))
+    xh = O.normal(c["length"] * c["count"], c["seed"], c["mean"], c["std"]).reshape(
+        c["count"], c["length"])
+    assert sha(xh) == c["sha256_input"]
+    y = ops.softmax(torch.from_numpy(xh).to(dev))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    st = softmax_vector_stats(got)
+    ref = g["stats"]
+    for j in range(3):
+        assert O.isapprox(st[:, j], ref[:, j], 1e-5), j
+    rel = np.abs(st - ref) / np.abs(ref)
+    assert rel.max() < 1e-4, rel.max()
+    for i, v in zip(c["sampled_vectors"], g["vectors"]):
+        assert O.isapprox(got[i], v, 1e-5), i
