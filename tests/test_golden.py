@@ -71,3 +71,31 @@ def test_oracle_matmul_matches_reference_tf32_kernel(case):
     else:
         got = AM[f"matmul_{M}x{N}x{K}"]
     assert O.max_rel(got, ref) < 1e-3
+
+
+SB = os.path.join(HERE, "ref_goldens_softmax_baseline.json")
+
+
+@pytest.mark.skipif(not os.path.exists(SB), reason="BASELINE-size softmax golden not generated")
+def test_oracle_softmax_matches_reference_kernel_at_baseline_size():
+    """The oracle on the headline config (4096 vectors of 16384, 4*N(0,1))
+    against the reference's own softmax compiled with TILE = 16384: the
+    regenerated input is bit-identical (sha256), every vector's checksums
+    and four whole vectors agree within rtol 1e-5."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("make_goldens",
+                                                  os.path.join(HERE, "make_goldens.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    c = json.load(open(SB))
+    g = np.load(SB.replace(".json", ".npz"))
+    x = O.normal(c["length"] * c["count"], c["seed"], c["mean"], c["std"]).reshape(
+        c["count"], c["length"])
+    assert sha(x) == c["sha256_input"]
+    got = O.softmax(x)
+    st = mg.softmax_vector_stats(got)
+    for j in range(3):
+        assert O.isapprox(st[:, j], g["stats"][:, j], 1e-5), j
+    for i, v in zip(c["sampled_vectors"], g["vectors"]):
+        assert O.isapprox(got[i], v, 1e-5), i
