@@ -53,6 +53,18 @@ constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 #define CTB_FMHA_P_PARTS 2
 #endif
 constexpr int P_PARTS = CTB_FMHA_P_PARTS;     // P published in this many key ranges per block
+static_assert(P_PARTS == 1 || P_PARTS == 2 || P_PARTS == 4, "P is published in 1, 2 or 4 parts");
+static_assert(BKV / 16 % P_PARTS == 0, "each part must hold whole 16-key MMA steps");
+// Exponentials: 0 = Float32 MUFU ex2 (pairs via CTB_FMHA_EMU_EVERY on the FMA
+// pipe), 2 = Float16 pairs (ex2.approx.f16x2) with Float16 partial row sums
+// folded into Float32 every 64 keys. 1 is a timing probe without exponentials
+// (wrong results; never the default).
+#ifndef CTB_FMHA_EXP_MODE
+#define CTB_FMHA_EXP_MODE 0
+#endif
+#ifndef CTB_FMHA_HEAD_MAJOR
+#define CTB_FMHA_HEAD_MAJOR 1
+#endif
 constexpr unsigned ERR_BIT = 2u;
 
 struct Params {
@@ -66,6 +78,23 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Float16 pair helpers: lo in the low half, hi in the high half.
+__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -128,6 +157,17 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 // are 0/1 softmax tile t got S (t = 0, 1), 2/3 softmax tile t arrived P,
 // 4/5 MMA issued P_t*V, 6/7 MMA issued S_t(j+1), 8 MMA got V.
 __device__ long long g_fmha_trace[13][128];  // 9-12: completion of PV0, S0', PV1, S1'
+__device__ long long g_fmha_mma[4][9];  // block 30 of CTA 0: stamps around each MMA issue
+__device__ long long g_fmha_clk[4];     // CTA 0, thread 0: clock64 / globaltimer at start and end
+__device__ long long g_fmha_sm[2][10];  // CTA 0 block 30, first thread of each softmax tile
+#define FMHA_SM_STAMP(t, i, j)                                                               \
+  do {                                                                                     \
+    if (blockIdx.x == 0 && (j) == 30 && threadIdx.x % 128 == 0) g_fmha_sm[(t)][(i)] = clock64(); \
+  } while (0)
+#define FMHA_MMA_STAMP(g, i, on)                                          \
+  do {                                                                    \
+    if ((on) && blockIdx.x == 0) g_fmha_mma[(g)][(i)] = clock64();        \
+  } while (0)
 #define FMHA_TRACE(ev, j)                                                      \
   do {                                                                       \
     if (blockIdx.x == 0 && (j) < 128) g_fmha_trace[(ev)][(j)] = clock64();   \
@@ -135,6 +175,12 @@ __device__ long long g_fmha_trace[13][128];  // 9-12: completion of PV0, S0', PV
 #else
 #define FMHA_TRACE(ev, j) \
   do {                    \
+  } while (0)
+#define FMHA_MMA_STAMP(g, i, on) \
+  do {                           \
+  } while (0)
+#define FMHA_SM_STAMP(t, i, j) \
+  do {                         \
   } while (0)
 #endif
 
@@ -151,15 +197,17 @@ constexpr int EMU_EVERY = CTB_FMHA_EMU_EVERY;
 // S_t = Q_t K^T for one key block: 8 MMAs of K = 16 over head_dim, Q and K
 // both K-major 128-byte-swizzled (two 64-wide boxes of 16 KB each).
 __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sKa, int t,
-                                        int stage, uint64_t* s_full_t) {
+                                        int stage, uint64_t* s_full_t, bool tr = false) {
   using namespace sm100;
   constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV, false, false);
   const uint32_t qa = sQa + t * TILE_BYTES, ka = sKa + stage * TILE_BYTES;
+  FMHA_MMA_STAMP(2 * t, 0, tr);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
     mma_f16_ss_elect(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
                smem_desc_sw128(ka + off, 16, 1024), idesc_s, kk != 0);
+    FMHA_MMA_STAMP(2 * t, kk + 1, tr);
   }
   mma_commit_elect(s_full_t);
 }
@@ -168,7 +216,7 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
 // columns 0-63; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
 // 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
 __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j,
-                                         int part) {
+                                         int part, bool tr = false) {
   using namespace sm100;
   constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
   constexpr int STEPS = BKV / 16 / P_PARTS;  // 16-key MMA steps per published part
@@ -176,9 +224,11 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
 #pragma unroll
   for (int k4 = 0; k4 < STEPS; ++k4) {
     const int kk = part * STEPS + k4;
+    if (kk == 0) FMHA_MMA_STAMP(2 * t + 1, 0, tr);
     mma_f16_ts_elect(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
                      smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
                      (j > 0 || kk > 0) ? 1u : 0u);
+    FMHA_MMA_STAMP(2 * t + 1, kk + 1, tr);
   }
 }
 
@@ -209,10 +259,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // Heaviest (latest, for causal) query blocks first.
+#ifdef CTB_FMHA_TRACE
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    g_fmha_clk[0] = clock64();
+    g_fmha_clk[1] = (long long)global_ns();
+  }
+#endif
+  // CTAs of one (batch, head) are adjacent, so the CTAs resident at a time
+  // share a few heads' K and V through L2 instead of streaming one head
+  // each from HBM; within a head the heaviest (latest, for causal) query
+  // blocks go first.
   const int lin = blockIdx.x;
+#if CTB_FMHA_HEAD_MAJOR
+  const int bh = lin / p.n_qblk;
+  const int qblk = p.n_qblk - 1 - lin % p.n_qblk;
+#else
   const int qblk = p.n_qblk - 1 - lin / p.BH;
   const int bh = lin % p.BH;
+#endif
   const int q0 = qblk * 2 * BQ;
   int nb = (p.Sk + BKV - 1) / BKV;
   if (p.causal) nb = min(nb, (q0 + 2 * BQ + BKV - 1) / BKV);
@@ -295,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int q = 0; q < P_PARTS && ok; ++q) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[q], j & 1, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
-          issue_pv(tmem, sVa, 0, s, j, q);
+          issue_pv(tmem, sVa, 0, s, j, q, lane == 0 && j == 30);
         }
         if (!ok) break;
 #ifdef CTB_FMHA_TRACE
@@ -305,7 +369,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (more) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
-          issue_s(tmem, sQa, sKa, 0, sn, &s_full[0]);
+          issue_s(tmem, sQa, sKa, 0, sn, &s_full[0], lane == 0 && j == 30);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[1]);
 #endif
@@ -314,7 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int q = 0; q < P_PARTS && ok; ++q) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[P_PARTS + q], j & 1, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
-          issue_pv(tmem, sVa, 1, s, j, q);
+          issue_pv(tmem, sVa, 1, s, j, q, lane == 0 && j == 30);
         }
         if (!ok) break;
 #ifdef CTB_FMHA_TRACE
@@ -323,7 +387,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) FMHA_TRACE(5, j);
         mma_commit_elect(&v_empty[s]);
         if (more) {
-          issue_s(tmem, sQa, sKa, 1, sn, &s_full[1]);
+          issue_s(tmem, sQa, sKa, 1, sn, &s_full[1], lane == 0 && j == 30);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[3]);
 #endif
@@ -360,6 +424,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < nb; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag, ERR_BIT)) break;
       if (threadIdx.x % 128 == 0) FMHA_TRACE(t, j);
+      FMHA_SM_STAMP(t, 0, j);
       tc_fence_after();
       uint32_t r[4][32];
 #pragma unroll
@@ -367,6 +432,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int k0 = j * BKV;
       const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > q0 + t * BQ);
       tmem_ld_wait();
+      FMHA_SM_STAMP(t, 1, j);
       if (need_mask) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -386,6 +452,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         mx[c] = fmaxf(mx[c], __uint_as_float(r[c][31]));
       }
       const float m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+      FMHA_SM_STAMP(t, 2, j);
       float factor = 1.f;
       bool rescale = false;
       if (j == 0) {
@@ -409,6 +476,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st_32x32b_x16(o_col + c * 16, o);
         }
       }
+      FMHA_SM_STAMP(t, 3, j);
       // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
       // (-inf) - (-inf) would be NaN, so shift by 0 for them.
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
@@ -416,6 +484,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
       // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read
       // above. Each half (keys 0-63, 64-127) is published as soon as it is stored.
+#if CTB_FMHA_EXP_MODE == 2
+      uint32_t hacc[4] = {0u, 0u, 0u, 0u};  // f16x2 partial row sums, 8 values each
+#endif
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -426,18 +497,40 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     sl2x2, nm2);
           float xa, xb;
           f2_unpack(x, xa, xb);
+#if CTB_FMHA_EXP_MODE == 2
+          // exponentials of the pair in Float16 (P is Float16 for the P*V MMA)
+          const uint32_t e = ex2_f16x2(cvt_f16x2(xa, xb));
+          pk[i] = e;
+          hacc[i & 3] = hadd2(hacc[i & 3], e);
+#else
           uint64_t e;
+#if CTB_FMHA_EXP_MODE == 1
+          e = x;  // timing probe only: no exponentials (wrong results)
+#else
           if (!need_mask && (i % EMU_EVERY) == EMU_EVERY - 1)
             e = exp2_poly2(f2_pack(fmaxf(xa, -126.f), fmaxf(xb, -126.f)));
           else
             e = f2_pack(ex2(xa), ex2(xb));
+#endif
           if (i & 1) acc1 = f2_add(acc1, e);
           else acc0 = f2_add(acc0, e);
           float ea, eb;
           f2_unpack(e, ea, eb);
           pk[i] = pack_half2(ea, eb);
+#endif
         }
+#if CTB_FMHA_EXP_MODE == 2
+        if (c & 1) {  // fold the f16x2 partial sums into Float32 every 64 keys
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hacc[h]));
+            acc0 = f2_add(acc0, f2_pack(f.x, f.y));
+            hacc[h] = 0u;
+          }
+        }
+#endif
         tmem_st_32x32b_x16(s_col + c * 16, pk);
+        FMHA_SM_STAMP(t, 4 + c, j);
         if ((c + 1) % (4 / P_PARTS) == 0) {
           tmem_st_wait();
           tc_fence_before();
@@ -448,6 +541,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       f2_unpack(acc0, s0, s1);
       f2_unpack(acc1, s2, s3);
       l += (s0 + s1) + (s2 + s3);
+      FMHA_SM_STAMP(t, 8, j);
       if (threadIdx.x % 128 == 0) FMHA_TRACE(2 + t, j);
     }
     // ------------------------------------------------------------ epilogue
@@ -482,6 +576,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#ifdef CTB_FMHA_TRACE
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    g_fmha_clk[2] = clock64();
+    g_fmha_clk[3] = (long long)global_ns();
+  }
+#endif
 }
 
 }  // namespace fmha
@@ -491,6 +591,15 @@ int fmha_take_device_error(unsigned int* out) { return take_device_error(out); }
 #ifdef CTB_FMHA_TRACE
 extern "C" int ctb_fmha_trace_read(long long* out) {
   return cudaMemcpyFromSymbol(out, fmha::g_fmha_trace, sizeof(fmha::g_fmha_trace)) == cudaSuccess ? 0 : -6;
+}
+extern "C" int ctb_fmha_trace_sm_read(long long* out) {
+  return cudaMemcpyFromSymbol(out, fmha::g_fmha_sm, sizeof(fmha::g_fmha_sm)) == cudaSuccess ? 0 : -6;
+}
+extern "C" int ctb_fmha_trace_clk_read(long long* out) {
+  return cudaMemcpyFromSymbol(out, fmha::g_fmha_clk, sizeof(fmha::g_fmha_clk)) == cudaSuccess ? 0 : -6;
+}
+extern "C" int ctb_fmha_trace_mma_read(long long* out) {
+  return cudaMemcpyFromSymbol(out, fmha::g_fmha_mma, sizeof(fmha::g_fmha_mma)) == cudaSuccess ? 0 : -6;
 }
 #endif
 
