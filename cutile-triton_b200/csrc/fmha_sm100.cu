@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 namespace ctb {
 
@@ -55,12 +56,14 @@ constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 constexpr int P_PARTS = CTB_FMHA_P_PARTS;     // P published in this many key ranges per block
 static_assert(P_PARTS == 1 || P_PARTS == 2 || P_PARTS == 4, "P is published in 1, 2 or 4 parts");
 static_assert(BKV / 16 % P_PARTS == 0, "each part must hold whole 16-key MMA steps");
-// Exponentials: 0 = Float32 MUFU ex2 (pairs via CTB_FMHA_EMU_EVERY on the FMA
-// pipe), 2 = Float16 pairs (ex2.approx.f16x2) with Float16 partial row sums
-// folded into Float32 every 64 keys. 1 is a timing probe without exponentials
-// (wrong results; never the default).
+// Timing probes (wrong results; never the default): 1 = no exponentials,
+// 3 = no exponentials and no TMEM traffic from the softmax warps. 0 = the kernel.
 #ifndef CTB_FMHA_EXP_MODE
 #define CTB_FMHA_EXP_MODE 0
+#endif
+// Timing probe (wrong results; never the default): 1 = skip the P*V MMAs, 2 = skip the S MMAs.
+#ifndef CTB_FMHA_SKIP
+#define CTB_FMHA_SKIP 0
 #endif
 #ifndef CTB_FMHA_HEAD_MAJOR
 #define CTB_FMHA_HEAD_MAJOR 1
@@ -78,23 +81,6 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Float16 pair helpers: lo in the low half, hi in the high half.
-__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t r;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
-  return r;
-}
-__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -156,7 +142,7 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 // Debug-only timeline of CTA 0 (clock64 cycles): [event][block] where events
 // are 0/1 softmax tile t got S (t = 0, 1), 2/3 softmax tile t arrived P,
 // 4/5 MMA issued P_t*V, 6/7 MMA issued S_t(j+1), 8 MMA got V.
-__device__ long long g_fmha_trace[13][128];  // 9-12: completion of PV0, S0', PV1, S1'
+__device__ long long g_fmha_trace[15][128];  // 9-12: completion of PV0, S0', PV1, S1'
 __device__ long long g_fmha_mma[4][9];  // block 30 of CTA 0: stamps around each MMA issue
 __device__ long long g_fmha_clk[4];     // CTA 0, thread 0: clock64 / globaltimer at start and end
 __device__ long long g_fmha_sm[2][10];  // CTA 0 block 30, first thread of each softmax tile
@@ -202,6 +188,10 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
   constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV, false, false);
   const uint32_t qa = sQa + t * TILE_BYTES, ka = sKa + stage * TILE_BYTES;
   FMHA_MMA_STAMP(2 * t, 0, tr);
+#if CTB_FMHA_SKIP == 2
+  mma_commit_elect(s_full_t);
+  return;  // timing probe: no S MMAs
+#endif
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
@@ -221,6 +211,9 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
   constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
   constexpr int STEPS = BKV / 16 / P_PARTS;  // 16-key MMA steps per published part
   const uint32_t va = sVa + stage * TILE_BYTES;
+#if CTB_FMHA_SKIP == 1
+  return;  // timing probe: no P*V MMAs
+#endif
 #pragma unroll
   for (int k4 = 0; k4 < STEPS; ++k4) {
     const int kk = part * STEPS + k4;
@@ -327,10 +320,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sK + s * TILE_BYTES + h * HALF_BYTES, &tmK, &k_full[s], h * 64, j * BKV, bh);
+        FMHA_TRACE(13, j);
         if (!mbar_wait_bounded(&v_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
         mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sV + s * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[s], h * 64, j * BKV, bh);
+        FMHA_TRACE(14, j);
       }
     }
   } else if (warp == MMA_WARP) {
@@ -428,7 +423,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_col + c * 32, r[c]);
+      for (int c = 0; c < 4; ++c) {
+#if CTB_FMHA_EXP_MODE == 3
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[c][i] = __float_as_uint((float)(i - lane));  // probe: no S read
+#else
+        tmem_ld_32x32b_x32(s_col + c * 32, r[c]);
+#endif
+      }
       const int k0 = j * BKV;
       const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > q0 + t * BQ);
       tmem_ld_wait();
@@ -484,12 +486,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
       // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read
       // above. Each half (keys 0-63, 64-127) is published as soon as it is stored.
-#if CTB_FMHA_EXP_MODE == 2
-      uint32_t hacc[4] = {0u, 0u, 0u, 0u};  // f16x2 partial row sums, 8 values each
-#endif
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
+        auto chunk = [&](auto emu_tag) {
+        constexpr bool emu = decltype(emu_tag)::value;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[c][2 * i]),
@@ -497,17 +498,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     sl2x2, nm2);
           float xa, xb;
           f2_unpack(x, xa, xb);
-#if CTB_FMHA_EXP_MODE == 2
-          // exponentials of the pair in Float16 (P is Float16 for the P*V MMA)
-          const uint32_t e = ex2_f16x2(cvt_f16x2(xa, xb));
-          pk[i] = e;
-          hacc[i & 3] = hadd2(hacc[i & 3], e);
-#else
           uint64_t e;
-#if CTB_FMHA_EXP_MODE == 1
+#if CTB_FMHA_EXP_MODE == 1 || CTB_FMHA_EXP_MODE == 3
           e = x;  // timing probe only: no exponentials (wrong results)
 #else
-          if (!need_mask && (i % EMU_EVERY) == EMU_EVERY - 1)
+          // `emu` is uniform over the chunk (masked blocks take the MUFU path
+          // for every pair), so the pair loop has no branches to schedule around.
+          if (emu && (i % EMU_EVERY) == EMU_EVERY - 1)
             e = exp2_poly2(f2_pack(fmaxf(xa, -126.f), fmaxf(xb, -126.f)));
           else
             e = f2_pack(ex2(xa), ex2(xb));
@@ -517,19 +514,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           float ea, eb;
           f2_unpack(e, ea, eb);
           pk[i] = pack_half2(ea, eb);
-#endif
         }
-#if CTB_FMHA_EXP_MODE == 2
-        if (c & 1) {  // fold the f16x2 partial sums into Float32 every 64 keys
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hacc[h]));
-            acc0 = f2_add(acc0, f2_pack(f.x, f.y));
-            hacc[h] = 0u;
-          }
-        }
-#endif
+        };
+        if (EMU_EVERY <= 16 && !need_mask)
+          chunk(std::integral_constant<bool, (EMU_EVERY <= 16)>{});
+        else
+          chunk(std::integral_constant<bool, false>{});
+#if CTB_FMHA_EXP_MODE < 3
         tmem_st_32x32b_x16(s_col + c * 16, pk);
+#else
+        if (pk[0] == 0x12345678u && pk[15] == 0x9abcdef0u) tmem_st_32x32b_x16(s_col + c * 16, pk);  // probe: no P write
+#endif
         FMHA_SM_STAMP(t, 4 + c, j);
         if ((c + 1) % (4 / P_PARTS) == 0) {
           tmem_st_wait();
