@@ -62,6 +62,9 @@ def _wl():
                       2 * 4 * 16384 * 4096 + 2 * 4 * 4096 + 2 * 4 * 16384),
         "layernorm_bwd": ("layernorm-bwd f32, 16384 rows x 4096 (dx, dw, db)", "GB/s", "hbm",
                           3 * 4 * 16384 * 4096 + 4 * 4 * 4096 + 2 * 4 * 16384),
+        "layernorm_bwd_noalloc": ("layernorm-bwd f32, 16384 rows x 4096, allocation-free entry "
+                                  "point (built-in dW/dB workspace)", "GB/s", "hbm",
+                                  3 * 4 * 16384 * 4096 + 4 * 4 * 4096 + 2 * 4 * 16384),
         "transpose": ("transpose f32 8192 x 8192 (extra: not a BASELINE config)", "GB/s", "hbm",
                       2 * 4 * 8192 * 8192),
         "gemm": ("f16 GEMM M=N=K=8192, f32 accumulate, f16 out", "TFLOP/s", "tensor",
@@ -78,8 +81,10 @@ def _wl():
 
 
 WORKLOADS = _wl()
-LAUNCHES_PER_STEP = {"layernorm_bwd": 2, "moe": 2}  # row pass + fold; row gather + GEMM
-SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "transpose", "gemm", "bgemm", "fmha", "fmha_causal", "moe"]
+LAUNCHES_PER_STEP = {"layernorm_bwd": 2, "layernorm_bwd_noalloc": 2, "moe": 2}  # row pass + fold; row gather + GEMM
+SUITE_ORDER = ["vadd", "rowsum", "softmax", "layernorm", "layernorm_bwd", "layernorm_bwd_noalloc",
+               "transpose", "gemm", "bgemm", "fmha", "fmha_causal", "moe"]
+NO_E2E_CPU = {"layernorm_bwd_noalloc"}  # same work as layernorm_bwd; only the device time differs
 
 
 def load_peaks():
@@ -119,7 +124,8 @@ class Case:
 
     # name -> (units the job splits into, alignment of a shard boundary)
     UNITS = {"softmax": (4096, 1), "vadd": (1 << 28, 1024), "rowsum": (131072, 64),
-             "layernorm": (16384, 1), "layernorm_bwd": (16384, 1), "transpose": (8192, 32),
+             "layernorm": (16384, 1), "layernorm_bwd": (16384, 1),
+             "layernorm_bwd_noalloc": (16384, 1), "transpose": (8192, 32),
              "gemm": (8192, 256), "bgemm": (32, 1), "fmha": (8, 1), "fmha_causal": (8, 1),
              "moe": (16384, 1)}
 
@@ -171,7 +177,7 @@ class Case:
             self.run_host = lambda hi_, ho: ops.layernorm_fwd_host(
                 hi_[0], hi_[1], hi_[2], 1e-5, ho[0], ho[1], ho[2], dev.index or 0)
             self.inputs, self.outputs = [x, w, b], [y, mu, rs]
-        elif name == "layernorm_bwd":
+        elif name in ("layernorm_bwd", "layernorm_bwd_noalloc"):
             x = ops.fill_normal(T.empty(u, 4096, device=dev), seed, offset=lo * 4096)
             dy = ops.fill_normal(T.empty(u, 4096, device=dev), seed + 3, offset=lo * 4096)
             w = ops.fill_normal(T.empty(4096, device=dev), seed + 1, 1.0, 0.1)
@@ -180,9 +186,12 @@ class Case:
             dx = T.empty_like(x)
             dw = T.empty(4096, device=dev)
             db = T.empty(4096, device=dev)
-            groups = ops.layernorm_bwd_groups(4096, u)
-            part_ws = T.empty(2 * groups * 4096, device=dev)
-            self.run = lambda: ops.layernorm_bwd(x, dy, w, mu, rs, dx, dw, db, part_ws, groups)
+            if name == "layernorm_bwd":
+                groups = ops.layernorm_bwd_groups(4096, u)
+                part_ws = T.empty(2 * groups * 4096, device=dev)
+                self.run = lambda: ops.layernorm_bwd(x, dy, w, mu, rs, dx, dw, db, part_ws, groups)
+            else:
+                self.run = lambda: ops.layernorm_bwd_noalloc(x, dy, w, mu, rs, dx, dw, db)
             self.inputs, self.outputs = [x, dy, w, mu, rs], [dx, dw, db]
         elif name == "transpose":
             x = ops.fill_uniform(T.empty(u, 8192, device=dev), seed, offset=lo * 8192)
@@ -477,6 +486,8 @@ def cpu_workload(name):
     threads = O.threads()
     rng = np.random.default_rng(0)
     scale = 1e9 if WORKLOADS[name][1] == "GB/s" else 1e12
+    if name == "layernorm_bwd_noalloc":  # the same computation on the CPU
+        name = "layernorm_bwd"
 
     def loop(fn, work_per_call):
         return fn, work_per_call / scale
@@ -682,7 +693,9 @@ def run_reference(args):
 # bench/examples.jl names and implementation labels of the suite workloads.
 RESULT_NAMES = {"vadd": ("vadd", "b200"), "rowsum": ("rowsum", "b200"),
                 "softmax": ("softmax", "b200"), "layernorm": ("layernorm", "b200 Fwd"),
-                "layernorm_bwd": ("layernorm", "b200 Bwd"), "transpose": ("transpose", "b200"),
+                "layernorm_bwd": ("layernorm", "b200 Bwd"),
+                "layernorm_bwd_noalloc": ("layernorm", "b200 Bwd noalloc"),
+                "transpose": ("transpose", "b200"),
                 "gemm": ("matmul", "b200"), "bgemm": ("batchmatmul", "b200"),
                 "fmha": ("fmha", "b200"), "fmha_causal": ("fmha", "b200 causal"),
                 "moe": ("moe", "b200")}
@@ -797,8 +810,9 @@ def run_ours(args):
             if name == head:
                 continue
             steps = args.suite_steps if not name.startswith("fmha") else max(3, args.suite_steps // 4)
-            suite[name] = measure(name, steps, max(3, args.warmup), True,
-                                  True, args.cpu_budget / 3, strong)
+            full = name not in NO_E2E_CPU
+            suite[name] = measure(name, steps, max(3, args.warmup), full,
+                                  full, args.cpu_budget / 3, strong)
             suite[name]["config"] = WORKLOADS[name][0]
     gather = None
     if args.gather and dist_on:

@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstring>
 #include <algorithm>
+#include <cuda.h>
 #include <mutex>
 
 namespace ctb {
@@ -149,6 +150,39 @@ extern "C" int ctb_init(int device) {
   cudaSetDevice(prev);
   return rc;
 }
+
+namespace ctb {
+// ---- per-context set-up --------------------------------------------------------
+using PFN_ctxGetCurrent = CUresult (*)(CUcontext*);
+using PFN_ctxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+int current_context_id(unsigned long long* id) {
+  // Since CUDA 12 cudaSetDevice makes the device's primary context current
+  // (creating it again after a cudaDeviceReset), so the ID is the live one.
+  int dev = 0;
+  CTB_CUDA_CHECK(cudaGetDevice(&dev));
+  CTB_CUDA_CHECK(cudaSetDevice(dev));
+  static PFN_ctxGetCurrent get_current = nullptr;
+  static PFN_ctxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_ctxGetCurrent>(fn);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_ctxGetId>(fn);
+  });
+  if (!get_current || !get_id)
+    return set_error(CTB_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId entry points unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS)
+    return set_error(CTB_ERR_CUDA, "no current CUDA context");
+  return CTB_OK;
+}
+}  // namespace ctb
 
 extern "C" int ctb_check_device(void* stream) {
   clear_error();

@@ -40,6 +40,11 @@ struct DeviceProps {
 // Properties of the current device (cached per device; ctb_init fills them).
 int current_props(DeviceProps* out);
 
+// Unique ID (never reused within a process) of the current device's primary
+// context. Per-device set-up (kernel attributes, symbol addresses) is
+// remembered with this ID, so after a cudaDeviceReset it is done again.
+int current_context_id(unsigned long long* id);
+
 // ---- device error word ------------------------------------------------------
 // Set by a kernel whose bounded wait gave up; read by ctb_check_device.
 // Bits: 1 = GEMM, 2 = FMHA, 4 = LayerNorm backward, 8 = MoE pipeline wait,

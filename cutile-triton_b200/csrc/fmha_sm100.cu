@@ -598,18 +598,20 @@ extern "C" int ctb_fmha_trace_mma_read(long long* out) {
 }
 #endif
 
-static bool g_fmha_attr_done[64];
+static unsigned long long g_fmha_attr_done[64];  // context ID the set-up was done in
 static std::mutex g_fmha_mu;
 
 int fmha_device_setup() {
   int dev = 0;
   CTB_CUDA_CHECK(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_fmha_mu);
-  if (dev < 64 && g_fmha_attr_done[dev]) return CTB_OK;
+  unsigned long long ctx = 0;
+  if (int rc = current_context_id(&ctx)) return rc;
+  if (dev < 64 && g_fmha_attr_done[dev] == ctx) return CTB_OK;
   CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_tcgen05_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       fmha::SMEM_BYTES));
-  if (dev < 64) g_fmha_attr_done[dev] = true;
+  if (dev < 64) g_fmha_attr_done[dev] = ctx;
   return CTB_OK;
 }
 

@@ -578,7 +578,7 @@ extern "C" int ctb_gemm_trace_read(unsigned long long* out) {
 }
 #endif
 
-static bool g_gemm_attr_done[64];
+static unsigned long long g_gemm_attr_done[64];  // context ID the set-up was done in
 static int g_gemm_pairs[64];
 static std::mutex g_gemm_mu;
 
@@ -586,7 +586,9 @@ int gemm_device_setup() {
   int dev = 0;
   CTB_CUDA_CHECK(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_gemm_mu);
-  if (dev < 64 && g_gemm_attr_done[dev]) return CTB_OK;
+  unsigned long long ctx = 0;
+  if (int rc = current_context_id(&ctx)) return rc;
+  if (dev < 64 && g_gemm_attr_done[dev] == ctx) return CTB_OK;
   CTB_CUDA_CHECK(cudaFuncSetAttribute(gemm::gemm_f16_tcgen05_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       gemm::SMEM_BYTES));
@@ -609,7 +611,7 @@ int gemm_device_setup() {
   CTB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16_pair_kernel, &cfg));
   if (dev < 64) {
     g_gemm_pairs[dev] = clusters;
-    g_gemm_attr_done[dev] = true;
+    g_gemm_attr_done[dev] = ctx;
   }
   return CTB_OK;
 }

@@ -294,11 +294,14 @@ extern "C" int ctb_layernorm_bwd_f32(const float* x, const float* dy, const floa
 // GPU that loads the library until the process exits. In host code its name
 // is only a host-side stand-in, so its device address is fetched per device
 // with cudaGetSymbolAddress on the first call made on that device (with that
-// device current); make that first call before any stream capture. All calls
-// share the one array: two calls whose kernels overlap on a GPU (different
-// streams, or different host threads on one device) race and corrupt each
-// other's dW/dB. Each call writes every partial row it later reads, so no
-// clearing is needed between calls.
+// device current); make that first call before any stream capture. The
+// address is remembered together with the CUDA context's unique ID, so after
+// a cudaDeviceReset (a new primary context, the module loaded again) the next
+// call looks it up again instead of using a stale address. All calls share
+// the one array: two calls whose kernels overlap on a GPU (different streams,
+// or different host threads on one device) race and corrupt each other's
+// dW/dB. Each call writes every partial row it later reads, so no clearing
+// is needed between calls.
 // =============================================================================
 namespace ctb {
 
@@ -307,17 +310,21 @@ static __device__ __align__(256) float g_lnbwd_noalloc_scratch[LNBWD_NOALLOC_FLO
 
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[64];
+static unsigned long long g_noalloc_ctx[64];  // context ID the address belongs to
 
 static int noalloc_scratch(float** out) {
   int dev = 0;
   CTB_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return set_error(CTB_ERR_NO_DEVICE, "device ordinal out of range");
+  unsigned long long ctx = 0;
+  if (int rc = current_context_id(&ctx)) return rc;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (!g_noalloc_ptr[dev] || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_lnbwd_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(layernorm_bwd scratch)");
     g_noalloc_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return CTB_OK;

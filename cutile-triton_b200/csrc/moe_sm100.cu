@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(128) moe_gather_rows_kernel(const Params p, __
 
 int moe_take_device_error(unsigned int* out) { return take_device_error(out); }
 
-static bool g_moe_attr_done[64];
+static unsigned long long g_moe_attr_done[64];  // context ID the set-up was done in
 static int g_moe_pairs[64];
 static std::mutex g_moe_mu;
 
@@ -437,7 +437,9 @@ static int moe_device_setup() {
   int dev = 0;
   CTB_CUDA_CHECK(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_moe_mu);
-  if (dev < 64 && g_moe_attr_done[dev]) return CTB_OK;
+  unsigned long long ctx = 0;
+  if (int rc = current_context_id(&ctx)) return rc;
+  if (dev < 64 && g_moe_attr_done[dev] == ctx) return CTB_OK;
   CTB_CUDA_CHECK(cudaFuncSetAttribute(moe::moe_gemm_tcgen05_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       moe::SMEM_BYTES));
@@ -459,7 +461,7 @@ static int moe_device_setup() {
   CTB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&clusters, moe::moe_gemm_pair_kernel, &cfg));
   if (dev < 64) {
     g_moe_pairs[dev] = clusters;
-    g_moe_attr_done[dev] = true;
+    g_moe_attr_done[dev] = ctx;
   }
   return CTB_OK;
 }

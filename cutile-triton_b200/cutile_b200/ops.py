@@ -133,6 +133,18 @@ def layernorm_bwd(x, dy, w, mean, rstd, dx=None, dw=None, db=None, partial=None,
     return dx, dw, db
 
 
+def layernorm_bwd_noalloc(x, dy, w, mean, rstd, dx, dw, db, groups=0):
+    """LayerNorm backward through the allocation-free entry point: the dW/dB
+    workspace is the library's built-in array, so nothing is allocated on
+    the device here (every output must be passed in)."""
+    _need_cuda(x, dy, w, mean, rstd, dx, dw, db)
+    rows, n = x.shape
+    _lib.call("ctb_layernorm_bwd_f32_noalloc", x.data_ptr(), dy.data_ptr(), w.data_ptr(),
+              mean.data_ptr(), rstd.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), n,
+              rows, x.stride(0), dy.stride(0), dx.stride(0), int(groups), _st())
+    return dx, dw, db
+
+
 def transpose(x, out=None):
     """Julia y = x' on column-major storage: x_t (N, M) holds the Julia M x N
     matrix; returns y_t (M, N) holding the Julia N x M transpose."""

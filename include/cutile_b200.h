@@ -90,7 +90,8 @@ int ctb_init(int device);
 
 /* Reads and clears the device-side error word of the current device (set
  * when a bounded wait inside a kernel gave up). Synchronises `stream`.
- * Returns CTB_OK or CTB_ERR_TIMEOUT. */
+ * Returns CTB_OK or CTB_ERR_TIMEOUT; after CTB_ERR_TIMEOUT the outputs of
+ * the launches since the previous check are undefined. */
 int ctb_check_device(void* stream);
 
 /* ---- generic registry: the TritonRun.triton_kernel / launch! boundary ----- */
@@ -161,15 +162,18 @@ int ctb_layernorm_fwd_f32(const float* x, const float* w, const float* b,
  * and db partial rows, like the example's DW/DB group buffers; no locks are
  * needed). groups >= 1; ctb_layernorm_bwd_groups() gives the value that fills
  * the GPU. n <= 16384, n and the row strides multiples of 4, pointers
- * 16-byte aligned. Deterministic for a given `groups`. */
+ * 16-byte aligned. Deterministic for a given `groups`. If a bounded wait
+ * inside the row pass gives up (ctb_check_device then returns
+ * CTB_ERR_TIMEOUT), dx, dw and db of that call are undefined. */
 int ctb_layernorm_bwd_f32(const float* x, const float* dy, const float* w,
                           const float* mean, const float* rstd, float* dx,
                           float* dw, float* db, int32_t n, int32_t rows,
                           int64_t ldx, int64_t lddy, int64_t lddx,
                           float* partial, int32_t groups, void* stream);
 
-/* Recommended `groups` for ctb_layernorm_bwd_f32 on the current device
- * (2 x SM count, at most rows); -1 if the device cannot be queried. */
+/* Recommended `groups` for ctb_layernorm_bwd_f32 on the current device: one
+ * wave of resident CTAs — 4 per SM for n <= 2048, 1 per SM above that — at
+ * most rows; -1 if the device cannot be queried. */
 int ctb_layernorm_bwd_groups(int32_t n, int32_t rows);
 
 /* Allocation-free variant of ctb_layernorm_bwd_f32 (no counterpart in the
@@ -179,10 +183,15 @@ int ctb_layernorm_bwd_groups(int32_t n, int32_t rows);
  * be entered. The dW/dB partial workspace comes from a 4 MiB array built
  * into the library (held on every GPU that loads it until exit) instead of
  * from the caller; the caller still passes every input and output.
- * groups <= 0 picks the largest useful value that fits; 2 * groups * n must
+ * groups <= 0 picks the largest useful value that fits: the value of
+ * ctb_layernorm_bwd_groups capped at 1,048,576 / (2 * n) (128 at n = 4096,
+ * where ctb_layernorm_bwd_groups gives 148 on B200), so its dW/dB can differ
+ * from ctb_layernorm_bwd_f32's in the last bits (another summation order);
+ * pass the same `groups` to both for identical results. 2 * groups * n must
  * not exceed 1,048,576 floats (CTB_ERR_SHAPE otherwise). The first call on a
- * device looks up the array's device address; make it before any stream
- * capture. All calls share the array: calls that overlap on a GPU race. */
+ * device (and the first after a cudaDeviceReset) looks up the array's device
+ * address; make it before any stream capture. All calls share the array:
+ * calls that overlap on a GPU race. */
 int ctb_layernorm_bwd_f32_noalloc(const float* x, const float* dy,
                                   const float* w, const float* mean,
                                   const float* rstd, float* dx, float* dw,

@@ -6,8 +6,9 @@ is already reserved for its own pool, or Julia code where CUDA.jl's
 allocator must not be entered). Its dW/dB workspace is a fixed array inside
 the library, shared by every call, so this test makes two calls in a row with
 different shapes and checks each against the regular entry point
-(ctb_layernorm_bwd_f32, caller-provided workspace) at the tolerance the other
-layernorm tests use (Julia isapprox, rtol 1e-5). This file is collected last.
+(ctb_layernorm_bwd_f32, caller-provided workspace) and against the CPU oracle,
+at the tolerance the other layernorm tests use (Julia isapprox, rtol 1e-5).
+This file is collected last.
 """
 import ctypes
 
@@ -50,6 +51,10 @@ def test_noalloc_matches_regular_entry_point_twice(dev):
         torch.cuda.synchronize()
         for got, ref in ((dx, rdx), (dw, rdw), (db, rdb)):
             assert O.isapprox(got.cpu().numpy(), ref.cpu().numpy(), 1e-5)
+        # and directly against the CPU oracle (float64 accumulation)
+        odx, odw, odb = O.layernorm_bwd(*(t.cpu().numpy() for t in (x, dy, w, mu, rs)))
+        for got, ref in ((dx, odx), (dw, odw), (db, odb)):
+            assert O.isapprox(got.cpu().numpy(), ref, 1e-5)
 
 
 def test_noalloc_rejects_workspace_beyond_the_built_in_array(dev):
