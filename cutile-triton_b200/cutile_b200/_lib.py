@@ -87,6 +87,8 @@ SIGNATURES = {
                       _P],
     "ctb_fmha_fwd_f16": [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P],
     "ctb_moe_workspace_bytes": [_I32, _I32],
+    "ctb_moe_align_capacity": [_I32, _I32, _I32],
+    "ctb_moe_align_i32": [_P, _I32, _I32, _I32, _P, _P, _P, _I32, _P],
     "ctb_host_workspace_bytes": [_I64, _I64, _I64],
     "ctb_softmax_f32_host": [_P, _P, _I32, _I32, _P, _I64, _P],
     "ctb_layernorm_fwd_f32_host": [_P, _P, _P, _P, _P, _P, _I32, _I32, _F, _P, _I64, _P],

@@ -206,7 +206,28 @@ def moe_align(topk_ids, num_experts, block=MOE_BLOCK):
     """Routing in the fused-MoE layout: returns (sorted_token_ids int32 [EM],
     expert_ids int32 [EM/block], num_tokens_post_padded int32 [1]) on the
     device of `topk_ids` ((M, topk) int tensor). Slots of each expert are
-    listed in token order and padded to a multiple of `block` with M*topk."""
+    listed in token order and padded to a multiple of `block` with M*topk.
+
+    On a CUDA tensor this is one device kernel (ctb_moe_align_i32) and never
+    waits for the GPU: EM is the worst case for the routing
+    (ctb_moe_align_capacity), entries past num_tokens_post_padded hold the
+    padding id and blocks past it expert -1, which the MoE GEMM skips. On a
+    host tensor the exact-size layout is computed on the host."""
+    if topk_ids.is_cuda:
+        n = topk_ids.numel()
+        ids = topk_ids.reshape(-1)
+        if ids.dtype != torch.int32:
+            ids = ids.to(torch.int32)
+        ids = ids.contiguous()
+        cap = int(_lib.load().ctb_moe_align_capacity(n, num_experts, block))
+        if cap < 0:
+            _lib.check(-3)
+        sorted_ids = torch.empty(cap, dtype=torch.int32, device=ids.device)
+        expert_ids = torch.empty(cap // block, dtype=torch.int32, device=ids.device)
+        ntp = torch.empty(1, dtype=torch.int32, device=ids.device)
+        _lib.call("ctb_moe_align_i32", ids.data_ptr(), n, num_experts, block,
+                  sorted_ids.data_ptr(), expert_ids.data_ptr(), ntp.data_ptr(), cap, _st())
+        return sorted_ids, expert_ids, ntp
     flat = topk_ids.reshape(-1).to(torch.int64)
     n = flat.numel()
     counts = torch.bincount(flat, minlength=num_experts)

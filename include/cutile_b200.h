@@ -266,6 +266,23 @@ int ctb_vadd_host(int32_t dtype, const void* a, const void* b, void* c, int64_t 
  * `workspace` (16-byte aligned, at least ctb_moe_workspace_bytes(EM, K))
  * receives the routed rows of A in sorted order before the GEMM runs. */
 int64_t ctb_moe_workspace_bytes(int32_t EM, int32_t K);
+
+/* Routing for ctb_moe_gemm_f16 on the device, without a host round trip:
+ * the `moe_align_block_size` step of the fused-MoE contract (the layout the
+ * cuTile moe example consumes; the example is not vendored in the
+ * reference). topk_ids: `slots` = M * topk Int32 expert ids in slot order
+ * (token-major). Writes sorted_token_ids[capacity] (each expert's slots in
+ * slot order, padded with the id `slots` to a multiple of `block`, experts
+ * in order, then `slots` up to capacity), expert_ids[capacity / block] (-1
+ * past the last used block) and num_tokens_post_padded[1]. capacity must be
+ * a multiple of block and at least ctb_moe_align_capacity(slots, E, block),
+ * the worst case, so the caller sizes the outputs without knowing the
+ * routing; pass EM = capacity to ctb_moe_gemm_f16. E <= 256. Ids outside
+ * [0, E) are not listed. One CTA; runs on `stream`. */
+int32_t ctb_moe_align_capacity(int32_t slots, int32_t E, int32_t block);
+int ctb_moe_align_i32(const int32_t* topk_ids, int32_t slots, int32_t E, int32_t block,
+                      int32_t* sorted_token_ids, int32_t* expert_ids,
+                      int32_t* num_tokens_post_padded, int32_t capacity, void* stream);
 int ctb_moe_gemm_f16(const void* A, const void* B, void* C,
                      const int32_t* sorted_token_ids, const int32_t* expert_ids,
                      const int32_t* num_tokens_post_padded,

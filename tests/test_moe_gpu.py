@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from cutile_b200 import ops
+from cutile_b200 import _lib, ops
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -52,12 +52,31 @@ def test_moe_gemm(dev, M, N, K, E, topk, weighted, skew, block):
 
 @pytest.mark.parametrize("block", [128, 256])
 def test_moe_align_matches_oracle_loops(dev, block):
-    ids = routing(333, 9, 3, 5, skew=True)
-    s, e, n = ops.moe_align(ids.to(dev), 9, block)
-    rs, re, rn = O.moe_align(ids.numpy(), 9, block)
-    np.testing.assert_array_equal(s.cpu().numpy(), rs)
-    np.testing.assert_array_equal(e.cpu().numpy(), re)
-    assert int(n.item()) == rn
+    """The device routing kernel against the oracle's loops: the oracle's
+    exact-size lists are a prefix of the worst-case-size device outputs, the
+    rest holds the padding id (sorted ids) and -1 (expert ids)."""
+    cases = [(333, 9, 3, 5, True), (1, 4, 1, 0, False), (7, 64, 4, 3, False),
+             (5000, 256, 2, 9, True), (2048, 8, 2, 11, False)]
+    for M, E, topk, seed, skew in cases:
+        ids = routing(M, E, topk, seed, skew=skew)
+        s, e, n = ops.moe_align(ids.to(dev), E, block)
+        rs, re, rn = O.moe_align(ids.numpy(), E, block)
+        s, e = s.cpu().numpy(), e.cpu().numpy()
+        cap = int(_lib.load().ctb_moe_align_capacity(M * topk, E, block))
+        assert s.size == cap and e.size == cap // block
+        np.testing.assert_array_equal(s[:rs.size], rs)
+        assert np.all(s[rs.size:] == M * topk)
+        np.testing.assert_array_equal(e[:re.size], re)
+        assert np.all(e[re.size:] == -1)
+        assert int(n.item()) == rn
+
+
+def test_moe_align_empty_and_errors(dev):
+    ids = torch.empty(0, 2, dtype=torch.int32, device=dev)
+    s, e, n = ops.moe_align(ids, 4, 128)
+    assert int(n.item()) == 0 and bool((e.cpu() == -1).all()) and bool((s.cpu() == 0).all())
+    with pytest.raises(_lib.B200Error):
+        ops.moe_align(torch.zeros(4, 2, dtype=torch.int32, device=dev), 300, 128)
 
 
 @pytest.mark.parametrize("block", [128, 256])
@@ -141,7 +160,7 @@ def test_moe_256_row_blocks_on_the_single_sm_kernel():
 import json, sys
 sys.path.insert(0, "cutile-triton_b200"); sys.path.insert(0, ".")
 import numpy as np, torch
-from cutile_b200 import ops
+from cutile_b200 import _lib, ops
 from oracle import oracle as O
 dev = torch.device("cuda", 0)
 A = ops.fill_uniform(torch.empty(700, 136, dtype=torch.float16, device=dev), 1)
