@@ -44,3 +44,21 @@ def test_algorithmic_work_per_launch():
     assert W["fmha_causal"][3] * 2 == W["fmha"][3]
     assert W["moe"][3] == 2 * 16384 * 2 * 14336 * 4096
     assert set(bench.SUITE_ORDER) == set(W)
+
+
+def test_strong_scaling_shards_cover_each_job_once():
+    """--scaling strong splits one BASELINE job: for 1, 2, 4 and 8 ranks the
+    rank shards of every workload are disjoint, cover all its units and keep
+    the alignment the kernels' fast paths want."""
+    import bench
+    from cutile_b200.shard import shard_range
+
+    for name, (total, align) in bench.Case.UNITS.items():
+        assert name in bench.WORKLOADS
+        for world in (1, 2, 4, 8):
+            got = [shard_range(total, r, world, align) for r in range(world)]
+            assert got[0][0] == 0 and got[-1][1] == total
+            for (lo, hi), (lo2, _) in zip(got, got[1:]):
+                assert hi == lo2 and lo <= hi
+            assert all(lo % align == 0 for lo, _ in got)
+            assert all(hi - lo > 0 for lo, hi in got), (name, world)
