@@ -307,6 +307,29 @@ function moe_align(topk_ids::AbstractMatrix{<:Integer}, num_experts::Integer; bl
     return sorted, experts, Int32[em]
 end
 
+"""
+    moe_align(topk_ids::CuMatrix{Int32}, num_experts; block=256)
+
+The same routing on the device (`ctb_moe_align_i32`), with no host round trip:
+the outputs are CuArrays sized for the worst case (`ctb_moe_align_capacity`);
+entries past num_tokens_post_padded hold the padding id and blocks past it the
+expert -1, which the `moe` kernel skips. At most 256 experts.
+"""
+function moe_align(topk_ids::CuMatrix{Int32}, num_experts::Integer; block::Integer=256)
+    n = length(topk_ids)
+    cap = ccall(sym(:ctb_moe_align_capacity), Int32, (Int32, Int32, Int32), n, num_experts, block)
+    cap < 0 && error("b200: moe_align: bad sizes")
+    sorted = CuArray{Int32}(undef, cap)
+    experts = CuArray{Int32}(undef, cap ÷ block)
+    ntp = CuArray{Int32}(undef, 1)
+    check(ccall(sym(:ctb_moe_align_i32), Cint,
+                (CuPtr{Int32}, Int32, Int32, Int32, CuPtr{Int32}, CuPtr{Int32}, CuPtr{Int32},
+                 Int32, Ptr{Cvoid}),
+                topk_ids, n, num_experts, block, sorted, experts, ntp, cap,
+                CUDA.stream().handle))
+    return sorted, experts, ntp
+end
+
 "Initialises the library on the active CUDA device (kernel attributes, checks sm_100)."
 function use_b200!()
     check(ccall(sym(:ctb_init), Cint, (Cint,), CUDA.deviceid(CUDA.device())))
