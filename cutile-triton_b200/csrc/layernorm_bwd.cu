@@ -290,7 +290,7 @@ extern "C" int ctb_layernorm_bwd_f32(const float* x, const float* dy, const floa
 // entry point takes the dW/dB partial workspace from a fixed array compiled
 // into the library instead of from the caller.
 //
-// The array below is LNBWD_NOALLOC_FLOATS floats (4 MiB) and lives on every
+// The array below is LNBWD_NOALLOC_FLOATS floats (8 MiB) and lives on every
 // GPU that loads the library until the process exits. In host code its name
 // is only a host-side stand-in, so its device address is fetched per device
 // with cudaGetSymbolAddress on the first call made on that device (with that
@@ -305,7 +305,7 @@ extern "C" int ctb_layernorm_bwd_f32(const float* x, const float* dy, const floa
 // =============================================================================
 namespace ctb {
 
-constexpr int64_t LNBWD_NOALLOC_FLOATS = 1 << 20;  // 4 MiB
+constexpr int64_t LNBWD_NOALLOC_FLOATS = 1 << 21;  // 8 MiB
 static __device__ __align__(256) float g_lnbwd_noalloc_scratch[LNBWD_NOALLOC_FLOATS];
 
 static std::mutex g_noalloc_mu;

@@ -180,15 +180,16 @@ int ctb_layernorm_bwd_groups(int32_t n, int32_t rows);
  * reference). For callers that cannot allocate device memory when they need
  * the backward pass — a process that reserved its whole device-memory budget
  * for its own pool, or Julia code running where CUDA.jl's allocator must not
- * be entered. The dW/dB partial workspace comes from a 4 MiB array built
+ * be entered. The dW/dB partial workspace comes from an 8 MiB array built
  * into the library (held on every GPU that loads it until exit) instead of
  * from the caller; the caller still passes every input and output.
  * groups <= 0 picks the largest useful value that fits: the value of
- * ctb_layernorm_bwd_groups capped at 1,048,576 / (2 * n) (128 at n = 4096,
- * where ctb_layernorm_bwd_groups gives 148 on B200), so its dW/dB can differ
- * from ctb_layernorm_bwd_f32's in the last bits (another summation order);
- * pass the same `groups` to both for identical results. 2 * groups * n must
- * not exceed 1,048,576 floats (CTB_ERR_SHAPE otherwise). The first call on a
+ * ctb_layernorm_bwd_groups capped at 2,097,152 / (2 * n) (256 at n = 4096, above
+ * the 148 that ctb_layernorm_bwd_groups gives there on B200); where the cap
+ * binds, dW/dB can differ from ctb_layernorm_bwd_f32's in the last bits
+ * (another summation order); pass the same `groups` to both for identical
+ * results. 2 * groups * n must
+ * not exceed 2,097,152 floats (CTB_ERR_SHAPE otherwise). The first call on a
  * device (and the first after a cudaDeviceReset) looks up the array's device
  * address; make it before any stream capture. All calls share the array:
  * calls that overlap on a GPU race. */

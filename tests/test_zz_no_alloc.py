@@ -59,6 +59,6 @@ def test_noalloc_matches_regular_entry_point_twice(dev):
 
 def test_noalloc_rejects_workspace_beyond_the_built_in_array(dev):
     x, dy, w, mu, rs = _case(dev, 2048, 4096, 90)
-    rc, *_ = _noalloc(x, dy, w, mu, rs, groups=1000)  # 2 x 1000 x 4096 floats > 1,048,576
+    rc, *_ = _noalloc(x, dy, w, mu, rs, groups=1000)  # 2 x 1000 x 4096 floats > 2,097,152
     assert rc == -3
     assert b"built-in scratch" in _lib.load().ctb_last_error()
