@@ -315,40 +315,126 @@ static int launch_softmax(const float* x, float* y, int len, int count, int64_t 
 // layernorm forward (cuTile example layernorm.jl:27; definitions of mean,
 // biased variance and rstd as stated in include/cutile_b200.h)
 // =============================================================================
-// One row per CTA trip; gamma/beta are read through the read-only path at
-// write-back time (32 KB shared by every CTA of the SM, so they hit L1/L2),
-// which keeps registers low and lets more rows be in flight per SM.
+// Merge of two partial (mean, M2) pairs over equal counts, each side holding
+// half of `total` elements (Chan, Golub and LeVeque 1979, pairwise update):
+// mean = (ma + mb) / 2, M2 = M2a + M2b + (mb - ma)^2 * total / 4. The sum is
+// written symmetrically so both lanes of an xor-shuffle pair get the same bits.
+__device__ __forceinline__ void chan_merge_equal(float& m, float& m2, float mo, float m2o,
+                                                 float total) {
+  const float d = mo - m;
+  m = 0.5f * (m + mo);
+  m2 = (m2 + m2o) + d * d * (0.25f * total);
+}
+
+// One row per CTA trip. Build-time options (measured in the design notes):
+// CTB_LN_WB_REG keeps this thread's gamma/beta columns in registers for the
+// whole launch instead of re-reading them through L1 for every row;
+// CTB_LN_AHEAD rows are loaded ahead of the row being reduced;
+// CTB_LN_FUSED merges (mean, M2) in one block reduction (Chan's update).
+#ifndef CTB_LN_WB_REG
+#define CTB_LN_WB_REG 0
+#endif
+#ifndef CTB_LN_AHEAD
+#define CTB_LN_AHEAD 1
+#endif
+#ifndef CTB_LN_FUSED
+#define CTB_LN_FUSED 0
+#endif
+#ifndef CTB_LN_CTA_THREADS
+#define CTB_LN_CTA_THREADS 1536  // resident threads per SM the bounds aim at (NV <= 2)
+#endif
+static_assert(CTB_LN_AHEAD == 1 || CTB_LN_AHEAD == 2, "rows loaded ahead: 1 or 2");
 template <int THREADS, int NV, bool VEC>
-__global__ void __launch_bounds__(THREADS, (THREADS >= 1024 ? 1 : (NV >= 4 ? 1024 : 1536) / THREADS))
+__global__ void __launch_bounds__(THREADS, (THREADS >= 1024 ? 1 : (NV >= 4 ? 1024 : CTB_LN_CTA_THREADS) / THREADS))
     layernorm_fwd_reg_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
     float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int n, int rows,
     int64_t ldx, int64_t ldy, float eps) {
+  constexpr int AHEAD = CTB_LN_AHEAD;
+  constexpr bool WB_REG = CTB_LN_WB_REG && VEC;
   __shared__ float red[THREADS / 32];
+  __shared__ float2 red2[2][THREADS / 32];  // by row parity: one barrier per row
   const float inv_n = 1.0f / (float)n;
   const int t = threadIdx.x;
-  // Software pipeline: the next row's loads are issued before this row's
-  // reductions, so two rows per CTA are in flight from HBM.
-  float nv[NV * 4];
-  if (blockIdx.x < rows) load_row<THREADS, NV, VEC>(x + (int64_t)blockIdx.x * ldx, n, 0.f, nv);
+  const bool full = CTB_LN_FUSED && VEC && n == THREADS * NV * 4;
+  int par = 0;
+  float4 wr[WB_REG ? NV : 1], br[WB_REG ? NV : 1];
+  if (WB_REG) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int idx0 = (k * THREADS + t) * 4;
+      wr[k] = idx0 < n ? __ldg(reinterpret_cast<const float4*>(w + idx0)) : make_float4(0, 0, 0, 0);
+      br[k] = idx0 < n ? __ldg(reinterpret_cast<const float4*>(b + idx0)) : make_float4(0, 0, 0, 0);
+    }
+  }
+  // Software pipeline: the next AHEAD rows' loads are issued before this
+  // row's reductions, so AHEAD + 1 rows per CTA are in flight from HBM.
+  float nv[AHEAD][NV * 4];
+#pragma unroll
+  for (int a = 0; a < AHEAD; ++a)
+    if (blockIdx.x + (int64_t)a * gridDim.x < rows)
+      load_row<THREADS, NV, VEC>(x + (blockIdx.x + (int64_t)a * gridDim.x) * ldx, n, 0.f, nv[a]);
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     float v[NV * 4];
 #pragma unroll
-    for (int i = 0; i < NV * 4; ++i) v[i] = nv[i];
-    if (row + gridDim.x < rows) load_row<THREADS, NV, VEC>(x + (row + gridDim.x) * ldx, n, 0.f, nv);
-    float s = 0.f;
+    for (int i = 0; i < NV * 4; ++i) v[i] = nv[0][i];
 #pragma unroll
-    for (int i = 0; i < NV * 4; ++i) s += v[i];
-    const float mu = block_reduce<THREADS / 32, false>(s, red) * inv_n;
-    float q = 0.f;
+    for (int a = 0; a + 1 < AHEAD; ++a)
 #pragma unroll
-    for (int k = 0; k < NV; ++k)
+      for (int i = 0; i < NV * 4; ++i) nv[a][i] = nv[a + 1][i];
+    const int64_t nxt = row + (int64_t)AHEAD * gridDim.x;
+    if (nxt < rows) load_row<THREADS, NV, VEC>(x + nxt * ldx, n, 0.f, nv[AHEAD - 1]);
+    float mu, var;
+    if (full) {
+      // Every thread holds NV*4 elements: per-thread (mean, M2), merged
+      // pairwise with Chan et al.'s update for equal counts, one barrier.
+      float lm = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float d = ((k * THREADS + t) * 4 + e < n) ? v[4 * k + e] - mu : 0.f;
-        q = fmaf(d, d, q);
+      for (int i = 0; i < NV * 4; ++i) lm += v[i];
+      lm *= 1.0f / (NV * 4);
+      float m2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV * 4; ++i) {
+        const float d = v[i] - lm;
+        m2 = fmaf(d, d, m2);
       }
-    const float var = block_reduce<THREADS / 32, false>(q, red) * inv_n;
+      float cnt = NV * 4;  // elements on each side of the next merge
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        chan_merge_equal(lm, m2, __shfl_xor_sync(0xffffffffu, lm, o),
+                         __shfl_xor_sync(0xffffffffu, m2, o), cnt * 2.f);
+        cnt *= 2.f;
+      }
+      float2* rb = red2[par];
+      if ((t & 31) == 0) rb[t >> 5] = make_float2(lm, m2);
+      __syncthreads();
+      float2 r = rb[(t & 31) % (THREADS / 32)];
+      lm = r.x;
+      m2 = r.y;
+#pragma unroll
+      for (int o = 1; o < THREADS / 32; o <<= 1) {
+        chan_merge_equal(lm, m2, __shfl_xor_sync(0xffffffffu, lm, o),
+                         __shfl_xor_sync(0xffffffffu, m2, o), cnt * 2.f);
+        cnt *= 2.f;
+      }
+      par ^= 1;
+      mu = lm;
+      var = m2 * inv_n;
+    } else {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV * 4; ++i) s += v[i];
+      mu = block_reduce<THREADS / 32, false>(s, red) * inv_n;
+      float q = 0.f;
+#pragma unroll
+      for (int k = 0; k < NV; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float d = ((k * THREADS + t) * 4 + e < n) ? v[4 * k + e] - mu : 0.f;
+          q = fmaf(d, d, q);
+        }
+      var = block_reduce<THREADS / 32, false>(q, red) * inv_n;
+    }
     const float rs = 1.0f / sqrtf(var + eps);
     float* yr = y + row * ldy;
 #pragma unroll
@@ -356,8 +442,8 @@ __global__ void __launch_bounds__(THREADS, (THREADS >= 1024 ? 1 : (NV >= 4 ? 102
       const int idx0 = (k * THREADS + t) * 4;
       if (VEC) {
         if (idx0 < n) {
-          const float4 wq = __ldg(reinterpret_cast<const float4*>(w + idx0));
-          const float4 bq = __ldg(reinterpret_cast<const float4*>(b + idx0));
+          const float4 wq = WB_REG ? wr[k] : __ldg(reinterpret_cast<const float4*>(w + idx0));
+          const float4 bq = WB_REG ? br[k] : __ldg(reinterpret_cast<const float4*>(b + idx0));
           st_stream_f4(yr + idx0, make_float4(fmaf((v[4 * k] - mu) * rs, wq.x, bq.x),
                                               fmaf((v[4 * k + 1] - mu) * rs, wq.y, bq.y),
                                               fmaf((v[4 * k + 2] - mu) * rs, wq.z, bq.z),
