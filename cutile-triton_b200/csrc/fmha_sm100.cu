@@ -225,6 +225,172 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
   }
 }
 
+// Softmax and epilogue of one query tile, one thread per query row (TMEM
+// lane): for each of the tile's nb key blocks, read S from TMEM, mask, update
+// the running max (rescaling O in TMEM when it moves), write P over S and
+// signal it per published part through `arrive_p(part)`; then normalise O
+// and store the row. `tile_row0` is the first query row of this CTA's part
+// of the tile (rows below it never need the causal mask for a block ending
+// at or before it).
+template <class ArriveP>
+__device__ __forceinline__ void softmax_rows(const Params& p, int t, uint32_t s_col,
+                                             uint32_t o_col, int qrow, int tile_row0, int bh,
+                                             int nb, uint64_t* s_full_t, uint64_t* o_full_t,
+                                             volatile int* abort_flag, ArriveP&& arrive_p) {
+  using namespace sm100;
+  [[maybe_unused]] const int lane = threadIdx.x % 32;  // timing probe only
+  const float sl2 = p.scale_log2;
+  float m_use = -INFINITY, l = 0.f;
+  for (int j = 0; j < nb; ++j) {
+    // Warp-uniform, so a warp never splits around the per-warp P arrivals.
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full_t, j & 1, abort_flag, ERR_BIT))) break;
+    if (threadIdx.x % 128 == 0) FMHA_TRACE(t, j);
+    FMHA_SM_STAMP(t, 0, j);
+    tc_fence_after();
+    uint32_t r[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#if CTB_FMHA_EXP_MODE == 3
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[c][i] = __float_as_uint((float)(i - lane));  // probe: no S read
+#else
+      tmem_ld_32x32b_x32(s_col + c * 32, r[c]);
+#endif
+    }
+    const int k0 = j * BKV;
+    const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > tile_row0);
+    tmem_ld_wait();
+    FMHA_SM_STAMP(t, 1, j);
+    if (need_mask) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = k0 + c * 32 + i;
+          if (key >= p.Sk || (p.causal && key > qrow)) r[c][i] = __float_as_uint(-INFINITY);
+        }
+    }
+    float mx[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      mx[c] = __uint_as_float(r[c][0]);
+#pragma unroll
+      for (int i = 1; i < 31; i += 2)
+        mx[c] = max3(mx[c], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+      mx[c] = fmaxf(mx[c], __uint_as_float(r[c][31]));
+    }
+    const float m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+    FMHA_SM_STAMP(t, 2, j);
+    float factor = 1.f;
+    bool rescale = false;
+    if (j == 0) {
+      m_use = m_blk;
+    } else if (m_blk > m_use + RESCALE_THRESHOLD) {
+      factor = ex2(m_use - m_blk);
+      l *= factor;
+      m_use = m_blk;
+      rescale = true;
+    }
+    if (__any_sync(0xffffffffu, rescale)) {
+      // O_t is stable here: P_t*V of block j-1 completed before S_t of block j,
+      // and P_t*V of block j waits for this thread's p_full arrivals below.
+#pragma unroll 1
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t o[16];
+        tmem_ld_32x32b_x16(o_col + c * 16, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+        tmem_st_32x32b_x16(o_col + c * 16, o);
+      }
+    }
+    FMHA_SM_STAMP(t, 3, j);
+    // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
+    // (-inf) - (-inf) would be NaN, so shift by 0 for them.
+    const float mref = (m_use == -INFINITY) ? 0.f : m_use;
+    const uint64_t sl2x2 = f2_pack(sl2, sl2), nm2 = f2_pack(-mref, -mref);
+    uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
+    // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read
+    // above. Each half (keys 0-63, 64-127) is published as soon as it is stored.
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t pk[16];
+      auto chunk = [&](auto emu_tag) {
+      constexpr bool emu = decltype(emu_tag)::value;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[c][2 * i]),
+                                          __uint_as_float(r[c][2 * i + 1])),
+                                  sl2x2, nm2);
+        float xa, xb;
+        f2_unpack(x, xa, xb);
+        uint64_t e;
+#if CTB_FMHA_EXP_MODE == 1 || CTB_FMHA_EXP_MODE == 3
+        e = x;  // timing probe only: no exponentials (wrong results)
+#else
+        // `emu` is uniform over the chunk (masked blocks take the MUFU path
+        // for every pair), so the pair loop has no branches to schedule around.
+        if (emu && (i % EMU_EVERY) == EMU_EVERY - 1)
+          e = exp2_poly2(f2_pack(fmaxf(xa, -126.f), fmaxf(xb, -126.f)));
+        else
+          e = f2_pack(ex2(xa), ex2(xb));
+#endif
+        if (i & 1) acc1 = f2_add(acc1, e);
+        else acc0 = f2_add(acc0, e);
+        float ea, eb;
+        f2_unpack(e, ea, eb);
+        pk[i] = pack_half2(ea, eb);
+      }
+      };
+      if (EMU_EVERY <= 16 && !need_mask)
+        chunk(std::integral_constant<bool, (EMU_EVERY <= 16)>{});
+      else
+        chunk(std::integral_constant<bool, false>{});
+#if CTB_FMHA_EXP_MODE < 3
+      tmem_st_32x32b_x16(s_col + c * 16, pk);
+#else
+      if (pk[0] == 0x12345678u && pk[15] == 0x9abcdef0u) tmem_st_32x32b_x16(s_col + c * 16, pk);  // probe: no P write
+#endif
+      FMHA_SM_STAMP(t, 4 + c, j);
+      if ((c + 1) % (4 / P_PARTS) == 0) {
+        tmem_st_wait();
+        tc_fence_before();
+        arrive_p(c / (4 / P_PARTS));
+      }
+    }
+    float s0, s1, s2, s3;
+    f2_unpack(acc0, s0, s1);
+    f2_unpack(acc1, s2, s3);
+    l += (s0 + s1) + (s2 + s3);
+    FMHA_SM_STAMP(t, 8, j);
+    if (threadIdx.x % 128 == 0) FMHA_TRACE(2 + t, j);
+  }
+  // ------------------------------------------------------------ epilogue
+  if (mbar_wait_bounded(o_full_t, 0, abort_flag, ERR_BIT)) {
+    tc_fence_after();
+    const float inv = 1.f / l;
+    __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld_32x32b_x32(o_col + c * 32, o);
+      tmem_ld_wait();
+      if (qrow < p.Sq) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack_half2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+          w.y = pack_half2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+          w.z = pack_half2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+          w.w = pack_half2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+          dst[v] = w;
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     fmha_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ,
                             const __grid_constant__ CUtensorMap tmK,
@@ -272,7 +438,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
   const int q0 = qblk * 2 * BQ;
   int nb = (p.Sk + BKV - 1) / BKV;
-  if (p.causal) nb = min(nb, (q0 + 2 * BQ + BKV - 1) / BKV);
+  // Causal: tile 1 needs the key blocks up to its last row, tile 0 one fewer
+  // (the block past its last row is fully masked for it and is skipped).
+  int nb0 = nb;
+  if (p.causal) {
+    nb = min(nb, (q0 + 2 * BQ + BKV - 1) / BKV);
+    nb0 = min(nb, (q0 + BQ + BKV - 1) / BKV);
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -351,12 +523,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT)))) break;
         if (lane == 0) FMHA_TRACE(8, j);
         // P*V on the first 64 keys starts while the softmax finishes the rest.
-        for (int q = 0; q < P_PARTS && ok; ++q) {
-          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[q], j & 1, abort_flag, ERR_BIT)))) break;
-          tc_fence_after();
-          issue_pv(tmem, sVa, 0, s, j, q, lane == 0 && j == 30);
+        if (j < nb0) {
+          for (int q = 0; q < P_PARTS && ok; ++q) {
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[q], j & 1, abort_flag, ERR_BIT)))) break;
+            tc_fence_after();
+            issue_pv(tmem, sVa, 0, s, j, q, lane == 0 && j == 30);
+          }
+          if (!ok) break;
+          if (j + 1 == nb0 && nb0 < nb) mma_commit_elect(&o_full[0]);  // tile 0 done early
         }
-        if (!ok) break;
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[0]);
 #endif
@@ -364,7 +539,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (more) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
-          issue_s(tmem, sQa, sKa, 0, sn, &s_full[0], lane == 0 && j == 30);
+          if (j + 1 < nb0) issue_s(tmem, sQa, sKa, 0, sn, &s_full[0], lane == 0 && j == 30);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[1]);
 #endif
@@ -390,7 +565,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           mma_commit_elect(&k_empty[sn]);
         }
       }
-      mma_commit_elect(&o_full[0]);
+      if (nb0 == nb) mma_commit_elect(&o_full[0]);
       mma_commit_elect(&o_full[1]);
     }
 #ifdef CTB_FMHA_TRACE
@@ -414,155 +589,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t s_col = tmem + lane_off + t * BKV;
     const uint32_t o_col = tmem + lane_off + 256 + t * D;
     const int qrow = q0 + t * BQ + quarter * 32 + lane;
-    const float sl2 = p.scale_log2;
-    float m_use = -INFINITY, l = 0.f;
-    for (int j = 0; j < nb; ++j) {
-      if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag, ERR_BIT)) break;
-      if (threadIdx.x % 128 == 0) FMHA_TRACE(t, j);
-      FMHA_SM_STAMP(t, 0, j);
-      tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#if CTB_FMHA_EXP_MODE == 3
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[c][i] = __float_as_uint((float)(i - lane));  // probe: no S read
-#else
-        tmem_ld_32x32b_x32(s_col + c * 32, r[c]);
-#endif
-      }
-      const int k0 = j * BKV;
-      const bool need_mask = (k0 + BKV > p.Sk) || (p.causal && k0 + BKV - 1 > q0 + t * BQ);
-      tmem_ld_wait();
-      FMHA_SM_STAMP(t, 1, j);
-      if (need_mask) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = k0 + c * 32 + i;
-            if (key >= p.Sk || (p.causal && key > qrow)) r[c][i] = __float_as_uint(-INFINITY);
-          }
-      }
-      float mx[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        mx[c] = __uint_as_float(r[c][0]);
-#pragma unroll
-        for (int i = 1; i < 31; i += 2)
-          mx[c] = max3(mx[c], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
-        mx[c] = fmaxf(mx[c], __uint_as_float(r[c][31]));
-      }
-      const float m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
-      FMHA_SM_STAMP(t, 2, j);
-      float factor = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m_use = m_blk;
-      } else if (m_blk > m_use + RESCALE_THRESHOLD) {
-        factor = ex2(m_use - m_blk);
-        l *= factor;
-        m_use = m_blk;
-        rescale = true;
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_t is stable here: P_t*V of block j-1 completed before S_t of block j,
-        // and P_t*V of block j waits for this thread's p_full arrivals below.
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t o[16];
-          tmem_ld_32x32b_x16(o_col + c * 16, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          tmem_st_32x32b_x16(o_col + c * 16, o);
-        }
-      }
-      FMHA_SM_STAMP(t, 3, j);
-      // Rows whose keys are all masked so far keep m_use = -inf; exp2 of
-      // (-inf) - (-inf) would be NaN, so shift by 0 for them.
-      const float mref = (m_use == -INFINITY) ? 0.f : m_use;
-      const uint64_t sl2x2 = f2_pack(sl2, sl2), nm2 = f2_pack(-mref, -mref);
-      uint64_t acc0 = 0, acc1 = 0;  // paired partial row sums (+0.0f bit patterns)
-      // P chunk c (16 packed columns) lands in columns [16c, 16c + 16), all read
-      // above. Each half (keys 0-63, 64-127) is published as soon as it is stored.
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-        auto chunk = [&](auto emu_tag) {
-        constexpr bool emu = decltype(emu_tag)::value;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[c][2 * i]),
-                                            __uint_as_float(r[c][2 * i + 1])),
-                                    sl2x2, nm2);
-          float xa, xb;
-          f2_unpack(x, xa, xb);
-          uint64_t e;
-#if CTB_FMHA_EXP_MODE == 1 || CTB_FMHA_EXP_MODE == 3
-          e = x;  // timing probe only: no exponentials (wrong results)
-#else
-          // `emu` is uniform over the chunk (masked blocks take the MUFU path
-          // for every pair), so the pair loop has no branches to schedule around.
-          if (emu && (i % EMU_EVERY) == EMU_EVERY - 1)
-            e = exp2_poly2(f2_pack(fmaxf(xa, -126.f), fmaxf(xb, -126.f)));
-          else
-            e = f2_pack(ex2(xa), ex2(xb));
-#endif
-          if (i & 1) acc1 = f2_add(acc1, e);
-          else acc0 = f2_add(acc0, e);
-          float ea, eb;
-          f2_unpack(e, ea, eb);
-          pk[i] = pack_half2(ea, eb);
-        }
-        };
-        if (EMU_EVERY <= 16 && !need_mask)
-          chunk(std::integral_constant<bool, (EMU_EVERY <= 16)>{});
-        else
-          chunk(std::integral_constant<bool, false>{});
-#if CTB_FMHA_EXP_MODE < 3
-        tmem_st_32x32b_x16(s_col + c * 16, pk);
-#else
-        if (pk[0] == 0x12345678u && pk[15] == 0x9abcdef0u) tmem_st_32x32b_x16(s_col + c * 16, pk);  // probe: no P write
-#endif
-        FMHA_SM_STAMP(t, 4 + c, j);
-        if ((c + 1) % (4 / P_PARTS) == 0) {
-          tmem_st_wait();
-          tc_fence_before();
-          mbar_arrive(&p_full[t * P_PARTS + c / (4 / P_PARTS)]);
-        }
-      }
-      float s0, s1, s2, s3;
-      f2_unpack(acc0, s0, s1);
-      f2_unpack(acc1, s2, s3);
-      l += (s0 + s1) + (s2 + s3);
-      FMHA_SM_STAMP(t, 8, j);
-      if (threadIdx.x % 128 == 0) FMHA_TRACE(2 + t, j);
-    }
-    // ------------------------------------------------------------ epilogue
-    if (mbar_wait_bounded(&o_full[t], 0, abort_flag, ERR_BIT)) {
-      tc_fence_after();
-      const float inv = 1.f / l;
-      __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(o_col + c * 32, o);
-        tmem_ld_wait();
-        if (qrow < p.Sq) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-            w.y = pack_half2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-            w.z = pack_half2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-            w.w = pack_half2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-            dst[v] = w;
-          }
-        }
-      }
-    }
+    softmax_rows(p, t, s_col, o_col, qrow, q0 + t * BQ, bh, t == 0 ? nb0 : nb, &s_full[t], &o_full[t], abort_flag,
+                 [&](int part) { mbar_arrive(&p_full[t * P_PARTS + part]); });
   }
 
   tc_fence_before();
@@ -577,6 +605,235 @@ __global__ void __launch_bounds__(THREADS, 1)
     g_fmha_clk[3] = (long long)global_ns();
   }
 #endif
+}
+
+
+// =============================================================================
+// CTA-pair variant (cta_group::2). A cluster of two CTAs on two SMs takes one
+// (batch*head, 512-query block) as two 256-row query tiles; tile t's rows
+// q0 + 256 t + 128 r + [0, 128) live in CTA r (its Q in shared memory, its S,
+// P and O in its own tensor memory, lanes = rows). Each CTA loads only half
+// of every key block's operands: keys [64 r, 64 r + 64) of K (the N half of
+// S = Q K^T) and head_dim columns [64 r, 64 r + 64) of V (the N half of
+// O += P V). The even CTA issues 256-row MMAs that read both CTAs' halves.
+// Per 128-key block an SM's shared memory then feeds 2 x 8 S steps of 6 KB
+// (against 8 KB on one SM) and 2 x 8 P*V steps of 2 KB, and receives 32 KB
+// of K/V (against 64 KB), so shared-memory bandwidth no longer paces the
+// tensor pipe. Roles per CTA are those of the one-SM kernel; the MMA warp
+// only issues in the even CTA, and the softmax warps of both CTAs arrive on
+// the even CTA's P barriers (one arrival per warp).
+// Barriers: q_full, k_full[s], v_full[s] and p_full live in the even CTA
+// and count both CTAs; k_empty, v_empty, s_full and o_full exist in both
+// CTAs and receive a commit each.
+// Causal: tile t only runs the key blocks that reach its last row.
+// =============================================================================
+#ifndef CTB_FMHA_PAIR_STAGES
+#define CTB_FMHA_PAIR_STAGES 4
+#endif
+constexpr int PR_STAGES = CTB_FMHA_PAIR_STAGES;    // K/V ring depth
+constexpr int PR_QROWS = 4 * BQ;                     // query rows per pair
+constexpr int PR_K_BYTES = 64 * D * 2;               // 64 keys x 128 head_dim: two 8 KB boxes
+constexpr int PR_K_BOX_BYTES = PR_K_BYTES / 2;
+constexpr int PR_V_BYTES = BKV * 64 * 2;             // 128 keys x 64 head_dim columns
+constexpr int PR_SMEM_BYTES = 2 * TILE_BYTES + PR_STAGES * (PR_K_BYTES + PR_V_BYTES) + 1024 + 512;
+static_assert(PR_SMEM_BYTES <= 232448, "pair FMHA shared memory exceeds the per-CTA limit");
+
+// S_t = Q_t K^T over the pair: M = 256 (128 rows per CTA), N = 128 keys (64 per CTA).
+__device__ __forceinline__ void issue_s_pair(uint32_t tmem, uint32_t sQa, uint32_t sKa, int t,
+                                             int stage, uint64_t* s_full_t) {
+  using namespace sm100;
+  constexpr uint32_t idesc_s = idesc_f16_f32(2 * BQ, BKV, false, false);
+  const uint32_t qa = sQa + t * TILE_BYTES, ka = sKa + stage * PR_K_BYTES;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t qoff = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+    const uint32_t koff = (kk >> 2) * PR_K_BOX_BYTES + (kk & 3) * 32;
+    mma_f16_ss_pair_elect(tmem + t * BKV, smem_desc_sw128(qa + qoff, 16, 1024),
+                          smem_desc_sw128(ka + koff, 16, 1024), idesc_s, kk != 0);
+  }
+  mma_commit_pair_both_elect(s_full_t);
+}
+
+// O_t (+)= P_t V for one published part of a key block: M = 256, N = 128
+// head_dim (64 per CTA, one 128-byte swizzle atom wide), 16 keys per step.
+__device__ __forceinline__ void issue_pv_pair(uint32_t tmem, uint32_t sVa, int t, int stage, int j,
+                                              int part) {
+  using namespace sm100;
+  constexpr uint32_t idesc_o = idesc_f16_f32(2 * BQ, D, false, true);
+  constexpr int STEPS = BKV / 16 / P_PARTS;
+  const uint32_t va = sVa + stage * PR_V_BYTES;
+#pragma unroll
+  for (int k4 = 0; k4 < STEPS; ++k4) {
+    const int kk = part * STEPS + k4;
+    mma_f16_ts_pair_elect(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
+                          smem_desc_sw128(va + kk * 2048, PR_V_BYTES, 1024), idesc_o,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fmha_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ,
+                         const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using namespace sm100;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                   // Q tiles 0, 1 (this CTA's rows)
+  uint8_t* sK = smem + 2 * TILE_BYTES;                  // PR_STAGES x 16 KB
+  uint8_t* sV = sK + PR_STAGES * PR_K_BYTES;            // PR_STAGES x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + PR_STAGES * PR_V_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;               // [PR_STAGES]
+  uint64_t* k_empty = k_full + PR_STAGES;      // [PR_STAGES]
+  uint64_t* v_full = k_empty + PR_STAGES;      // [PR_STAGES]
+  uint64_t* v_empty = v_full + PR_STAGES;      // [PR_STAGES]
+  uint64_t* s_full = v_empty + PR_STAGES;      // [2]
+  uint64_t* o_full = s_full + 2;               // [2]
+  uint64_t* p_full = o_full + 2;               // [2 tiles][P_PARTS]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_full + 2 * P_PARTS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int rank = (int)cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x / 2;
+  // Query blocks of one (batch, head) are adjacent pairs; heaviest first.
+  const int bh = pair / p.n_qblk;
+  const int qblk = p.n_qblk - 1 - pair % p.n_qblk;
+  const int q0 = qblk * PR_QROWS;
+  const int nb = (p.Sk + BKV - 1) / BKV;
+  int nbt[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+    nbt[t] = p.causal ? min(nb, (q0 + (t + 1) * 2 * BQ + BKV - 1) / BKV) : nb;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < PR_STAGES; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&o_full[i], 1);
+      for (int q = 0; q < P_PARTS; ++q) mbar_init(&p_full[P_PARTS * i + q], 2 * 4);  // 4 warps x 2 CTAs
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == MMA_WARP) tmem_alloc_pair(tmem_slot, 512);
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_OTHER));
+  if (warp == TMA_WARP) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t q_bar = mapa_shared(smem_u32(q_full), 0);
+      const uint32_t kf_bar = mapa_shared(smem_u32(k_full), 0);
+      const uint32_t vf_bar = mapa_shared(smem_u32(v_full), 0);
+      if (leader) mbar_arrive_expect_tx(q_full, 2 * 2 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d_pair(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_bar, h * 64,
+                           q0 + t * 2 * BQ + rank * BQ, bh);
+      for (int j = 0; j < nbt[1] && !*abort_flag; ++j) {
+        const int s = j % PR_STAGES;
+        const uint32_t ph = (j / PR_STAGES) & 1;
+        if (!mbar_wait_bounded(&k_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
+        if (leader) mbar_arrive_expect_tx(&k_full[s], 2 * PR_K_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d_pair(sK + s * PR_K_BYTES + h * PR_K_BOX_BYTES, &tmK, kf_bar + 8 * s, h * 64,
+                           j * BKV + rank * 64, bh);
+        if (!mbar_wait_bounded(&v_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
+        if (leader) mbar_arrive_expect_tx(&v_full[s], 2 * PR_V_BYTES);
+        tma_load_3d_pair(sV + s * PR_V_BYTES, &tmV, vf_bar + 8 * s, rank * 64, j * BKV, bh);
+      }
+    }
+  } else if (warp == MMA_WARP) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader) {
+      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+      bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(q_full, 0, abort_flag, ERR_BIT));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[0], 0, abort_flag, ERR_BIT));
+      if (ok) {
+        tc_fence_after();
+        issue_s_pair(tmem, sQa, sKa, 0, 0, &s_full[0]);
+        issue_s_pair(tmem, sQa, sKa, 1, 0, &s_full[1]);
+        mma_commit_pair_both_elect(&k_empty[0]);
+      }
+      // Per key block j: PV0(j) S0(j+1) PV1(j) S1(j+1), as on one SM; the pipe
+      // runs one thread's MMAs in order, so S_t(j+1) follows P_t(j)*V.
+      for (int j = 0; ok && j < nbt[1]; ++j) {
+        const int s = j % PR_STAGES, sn = (j + 1) % PR_STAGES;
+        const uint32_t ph = (j / PR_STAGES) & 1, phn = ((j + 1) / PR_STAGES) & 1;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&v_full[s], ph, abort_flag, ERR_BIT)))) break;
+        if (j < nbt[0]) {
+          for (int q = 0; q < P_PARTS && ok; ++q) {
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[q], j & 1, abort_flag, ERR_BIT)))) break;
+            tc_fence_after();
+            issue_pv_pair(tmem, sVa, 0, s, j, q);
+          }
+          if (!ok) break;
+          if (j + 1 == nbt[0]) mma_commit_pair_both_elect(&o_full[0]);
+        }
+        bool k_ready = false;
+        if (j + 1 < nbt[0]) {
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT)))) break;
+          k_ready = true;
+          tc_fence_after();
+          issue_s_pair(tmem, sQa, sKa, 0, sn, &s_full[0]);
+        }
+        for (int q = 0; q < P_PARTS && ok; ++q) {
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[P_PARTS + q], j & 1, abort_flag, ERR_BIT)))) break;
+          tc_fence_after();
+          issue_pv_pair(tmem, sVa, 1, s, j, q);
+        }
+        if (!ok) break;
+        mma_commit_pair_both_elect(&v_empty[s]);
+        if (j + 1 < nbt[1]) {
+          if (!k_ready) {
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT)))) break;
+            tc_fence_after();
+          }
+          issue_s_pair(tmem, sQa, sKa, 1, sn, &s_full[1]);
+          mma_commit_pair_both_elect(&k_empty[sn]);
+        }
+      }
+      mma_commit_pair_both_elect(&o_full[1]);
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax warpgroups (both CTAs)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFTMAX));
+    const int t = warp >> 2;
+    const int quarter = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + t * BKV;
+    const uint32_t o_col = tmem + lane_off + 256 + t * D;
+    const int row0 = q0 + t * 2 * BQ + rank * BQ;
+    const int qrow = row0 + quarter * 32 + lane;
+    const uint32_t p_bar = mapa_shared(smem_u32(&p_full[t * P_PARTS]), 0);
+    softmax_rows(p, t, s_col, o_col, qrow, row0, bh, nbt[t], &s_full[t], &o_full[t], abort_flag,
+                 [&](int part) {
+                   __syncwarp();
+                   if (lane == 0) mbar_arrive_cluster(p_bar + 8 * part);
+                 });
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its shared or tensor memory
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
 }
 
 }  // namespace fmha
@@ -599,7 +856,24 @@ extern "C" int ctb_fmha_trace_mma_read(long long* out) {
 #endif
 
 static unsigned long long g_fmha_attr_done[64];  // context ID the set-up was done in
+static int g_fmha_pairs[64];                     // resident CTA pairs of the pair kernel
 static std::mutex g_fmha_mu;
+
+static cudaLaunchConfig_t fmha_pair_config(cudaLaunchAttribute* attr, unsigned grid,
+                                           cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(fmha::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = fmha::PR_SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
 
 int fmha_device_setup() {
   int dev = 0;
@@ -611,16 +885,45 @@ int fmha_device_setup() {
   CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_tcgen05_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       fmha::SMEM_BYTES));
-  if (dev < 64) g_fmha_attr_done[dev] = ctx;
+  CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_pair_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      fmha::PR_SMEM_BYTES));
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = fmha_pair_config(attr, 2, 0);
+  int clusters = 0;
+  CTB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&clusters, fmha::fmha_fwd_pair_kernel, &cfg));
+  if (dev < 64) {
+    g_fmha_pairs[dev] = clusters;
+    g_fmha_attr_done[dev] = ctx;
+  }
   return CTB_OK;
+}
+
+// CTB_FMHA_PAIR=1 runs attention on the CTA-pair kernel (when a pair can be
+// resident). It is not the default: on B200 at B8 H32 S8192 D128 it measured
+// 980 / 830 TFLOP/s (non-causal / causal) against 1238 / 969 for the one-SM
+// kernel in the same process; both are paced by the per-tile chain S ->
+// softmax -> P*V -> next S, not by shared-memory bandwidth, and the pair adds
+// a cross-SM hand-off to every link of that chain.
+static bool fmha_use_pair() {
+  static const bool on = [] {
+    const char* e = getenv("CTB_FMHA_PAIR");
+    return e && e[0] == '1';
+  }();
+  if (!on) return false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  return g_fmha_pairs[dev] > 0;
 }
 
 static int fmha_tc(const __half* Q, const __half* K, const __half* V, __half* O, int B, int H,
                    int Sq, int Sk, float scale, int causal, cudaStream_t st) {
   if (int rc = fmha_device_setup()) return rc;
   const int BH = B * H;
+  const bool pair = fmha_use_pair();
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, 128, 1};
+  const uint32_t kbox[3] = {64, pair ? 64u : 128u, 1};  // a CTA of a pair loads 64 keys
   {
     const uint64_t dims[3] = {(uint64_t)fmha::D, (uint64_t)Sq, (uint64_t)BH};
     const uint64_t strides[2] = {(uint64_t)fmha::D * 2, (uint64_t)Sq * fmha::D * 2};
@@ -631,7 +934,7 @@ static int fmha_tc(const __half* Q, const __half* K, const __half* V, __half* O,
   {
     const uint64_t dims[3] = {(uint64_t)fmha::D, (uint64_t)Sk, (uint64_t)BH};
     const uint64_t strides[2] = {(uint64_t)fmha::D * 2, (uint64_t)Sk * fmha::D * 2};
-    if (int rc = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, K, dims, strides, box,
+    if (int rc = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, K, dims, strides, kbox,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
     if (int rc = encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, V, dims, strides, box,
@@ -646,6 +949,15 @@ static int fmha_tc(const __half* Q, const __half* K, const __half* V, __half* O,
   p.n_qblk = (Sq + 2 * fmha::BQ - 1) / (2 * fmha::BQ);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
+  if (pair) {
+    p.n_qblk = (Sq + fmha::PR_QROWS - 1) / fmha::PR_QROWS;
+    const int64_t grid = 2 * (int64_t)p.n_qblk * BH;
+    if (grid > 0x7fffffff) return set_error(CTB_ERR_SHAPE, "fmha: too many query blocks");
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = fmha_pair_config(attr, (unsigned)grid, st);
+    CTB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, fmha::fmha_fwd_pair_kernel, tq, tk, tv, p));
+    return launch_status("fmha_fwd_pair_kernel");
+  }
   const int64_t grid = (int64_t)p.n_qblk * BH;
   if (grid > 0x7fffffff) return set_error(CTB_ERR_SHAPE, "fmha: too many query blocks");
   fmha::fmha_fwd_tcgen05_kernel<<<(unsigned)grid, fmha::THREADS, fmha::SMEM_BYTES, st>>>(tq, tk,

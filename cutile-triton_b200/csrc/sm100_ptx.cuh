@@ -295,6 +295,19 @@ __device__ __forceinline__ void mma_f16_ss_pair_elect(uint32_t d_tmem, uint64_t 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Pair MMA with the A operand in tensor memory: each CTA supplies its own 128
+// rows of A from the same TMEM address of its own tensor memory.
+__device__ __forceinline__ void mma_f16_ts_pair_elect(uint32_t d_tmem, uint32_t a_tmem,
+                                                      uint64_t bdesc, uint32_t idesc,
+                                                      uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive once on `bar` (same shared-memory offset) in both CTAs of the pair
 // when this thread's previously issued pair MMAs finish: one commit to this
 // CTA's barrier and one to the peer's (its shared::cluster address); both
