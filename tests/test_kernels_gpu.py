@@ -135,7 +135,7 @@ def test_softmax_large_magnitude(dev):
 
 # ----------------------------------------------------------------------------- layernorm
 @pytest.mark.parametrize("rows,n", [(16384, 4096), (100, 1), (37, 7), (64, 4095), (8, 12288),
-                                    (4, 20000), (300, 512)])
+                                    (4, 20000), (300, 512), (33, 3000), (5, 2052), (1, 4096)])
 def test_layernorm_fwd(dev, rows, n):
     x = N((rows, n), 10, dev)
     w = N(n, 11, dev, mean=1.0, std=0.1)
