@@ -1,4 +1,5 @@
-// Attention forward on the 5th-generation tensor cores (tcgen05), head_dim 128.
+// Attention forward on the 5th-generation tensor cores (tcgen05), head_dim 64 or 128
+// (the one-SM kernel is a template on head_dim; the CTA-pair variant is 128 only).
 //
 // cuTile example fmha.jl:20 (not vendored in the reference; report.html:2981
 // describes its 4-D tiles with head_dim contiguous): O = softmax(scale*QK^T
@@ -15,7 +16,7 @@
 //   warp  9     TMA producer (one thread): Q once, then a 2-stage K / V ring
 //   warps 10-15 idle; with warps 8-9 they lend registers (setmaxnreg) so the
 //               softmax warps can run at 192 registers
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+HD) O1 [256+HD,256+2HD).
 // P_t (Float16, two per 32-bit column) overwrites S_t columns 0-63 once the
 // row's scores are in registers, and feeds P_t*V as the TMEM A operand.
 // Scores are kept in log2 units (exp2 with scale*log2(e) folded in). The
@@ -48,7 +49,10 @@ constexpr int THREADS = 16 * 32;
 constexpr int REG_SOFTMAX = 192, REG_OTHER = 64;
 constexpr int TILE_BYTES = BQ * D * 2;       // 32 KB: one 128 x 128 f16 tile
 constexpr int HALF_BYTES = TILE_BYTES / 2;   // one 64-wide (128-byte) TMA box
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr int BOX_BYTES = BQ * 64 * 2;       // one 128-row x 64-column TMA box (16 KB)
+// The one-SM kernel is built for head_dim HD = 64 or 128 (HD / 64 boxes per tile).
+template <int HD> __host__ __device__ constexpr int tile_bytes() { return BQ * HD * 2; }
+template <int HD> __host__ __device__ constexpr int smem_bytes() { return 6 * tile_bytes<HD>() + 1024 + 256; }
 constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 #ifndef CTB_FMHA_P_PARTS
 #define CTB_FMHA_P_PARTS 2
@@ -180,21 +184,22 @@ __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
 #endif
 constexpr int EMU_EVERY = CTB_FMHA_EMU_EVERY;
 
-// S_t = Q_t K^T for one key block: 8 MMAs of K = 16 over head_dim, Q and K
-// both K-major 128-byte-swizzled (two 64-wide boxes of 16 KB each).
+// S_t = Q_t K^T for one key block: HD/16 MMAs of K = 16 over head_dim, Q and
+// K both K-major 128-byte-swizzled (HD/64 boxes 64 wide, 16 KB each).
+template <int HD>
 __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sKa, int t,
                                         int stage, uint64_t* s_full_t, bool tr = false) {
   using namespace sm100;
   constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV, false, false);
-  const uint32_t qa = sQa + t * TILE_BYTES, ka = sKa + stage * TILE_BYTES;
+  const uint32_t qa = sQa + t * tile_bytes<HD>(), ka = sKa + stage * tile_bytes<HD>();
   FMHA_MMA_STAMP(2 * t, 0, tr);
 #if CTB_FMHA_SKIP == 2
   mma_commit_elect(s_full_t);
   return;  // timing probe: no S MMAs
 #endif
 #pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * BOX_BYTES + (kk & 3) * 32;
     mma_f16_ss_elect(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
                smem_desc_sw128(ka + off, 16, 1024), idesc_s, kk != 0);
     FMHA_MMA_STAMP(2 * t, kk + 1, tr);
@@ -205,12 +210,13 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t sQa, uint32_t sK
 // O_t (+)= P_t V for one half (64 keys) of a key block: P_t from TMEM (128 keys packed in S_t
 // columns 0-63; 16 keys = 8 columns per step), V as an MN-major B operand: 64-wide head_dim blocks at LBO = 16 KB,
 // 8-key groups at SBO = 1 KB, 16 keys per step = 2 KB.
+template <int HD>
 __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int stage, int j,
                                          int part, bool tr = false) {
   using namespace sm100;
-  constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D, false, true);
+  constexpr uint32_t idesc_o = idesc_f16_f32(BQ, HD, false, true);
   constexpr int STEPS = BKV / 16 / P_PARTS;  // 16-key MMA steps per published part
-  const uint32_t va = sVa + stage * TILE_BYTES;
+  const uint32_t va = sVa + stage * tile_bytes<HD>();
 #if CTB_FMHA_SKIP == 1
   return;  // timing probe: no P*V MMAs
 #endif
@@ -218,8 +224,8 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
   for (int k4 = 0; k4 < STEPS; ++k4) {
     const int kk = part * STEPS + k4;
     if (kk == 0) FMHA_MMA_STAMP(2 * t + 1, 0, tr);
-    mma_f16_ts_elect(tmem + 256 + t * D, tmem + t * BKV + kk * 8,
-                     smem_desc_sw128(va + kk * 2048, HALF_BYTES, 1024), idesc_o,
+    mma_f16_ts_elect(tmem + 256 + t * HD, tmem + t * BKV + kk * 8,
+                     smem_desc_sw128(va + kk * 2048, BOX_BYTES, 1024), idesc_o,
                      (j > 0 || kk > 0) ? 1u : 0u);
     FMHA_MMA_STAMP(2 * t + 1, kk + 1, tr);
   }
@@ -232,7 +238,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sVa, int t, int
 // and store the row. `tile_row0` is the first query row of this CTA's part
 // of the tile (rows below it never need the causal mask for a block ending
 // at or before it).
-template <class ArriveP>
+template <int HD, class ArriveP>
 __device__ __forceinline__ void softmax_rows(const Params& p, int t, uint32_t s_col,
                                              uint32_t o_col, int qrow, int tile_row0, int bh,
                                              int nb, uint64_t* s_full_t, uint64_t* o_full_t,
@@ -295,7 +301,7 @@ __device__ __forceinline__ void softmax_rows(const Params& p, int t, uint32_t s_
       // O_t is stable here: P_t*V of block j-1 completed before S_t of block j,
       // and P_t*V of block j waits for this thread's p_full arrivals below.
 #pragma unroll 1
-      for (int c = 0; c < D / 16; ++c) {
+      for (int c = 0; c < HD / 16; ++c) {
         uint32_t o[16];
         tmem_ld_32x32b_x16(o_col + c * 16, o);
         tmem_ld_wait();
@@ -369,9 +375,9 @@ __device__ __forceinline__ void softmax_rows(const Params& p, int t, uint32_t s_
   if (mbar_wait_bounded(o_full_t, 0, abort_flag, ERR_BIT)) {
     tc_fence_after();
     const float inv = 1.f / l;
-    __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * D;
+    __half* orow = p.O + ((int64_t)bh * p.Sq + qrow) * HD;
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = 0; c < HD / 32; ++c) {
       uint32_t o[32];
       tmem_ld_32x32b_x32(o_col + c * 32, o);
       tmem_ld_wait();
@@ -391,6 +397,7 @@ __device__ __forceinline__ void softmax_rows(const Params& p, int t, uint32_t s_
   }
 }
 
+template <int HD>
 __global__ void __launch_bounds__(THREADS, 1)
     fmha_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ,
                             const __grid_constant__ CUtensorMap tmK,
@@ -400,9 +407,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sQ = smem;                        // Q0, Q1
-  uint8_t* sK = smem + 2 * TILE_BYTES;       // 2 stages
-  uint8_t* sV = smem + 4 * TILE_BYTES;       // 2 stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES);
+  uint8_t* sK = smem + 2 * tile_bytes<HD>();       // 2 stages
+  uint8_t* sV = smem + 4 * tile_bytes<HD>();       // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * tile_bytes<HD>());
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -481,22 +488,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, 2 * tile_bytes<HD>());
       for (int t = 0; t < 2; ++t)
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * BQ, bh);
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sQ + t * tile_bytes<HD>() + h * BOX_BYTES, &tmQ, q_full, h * 64, q0 + t * BQ, bh);
       for (int j = 0; j < nb && !*abort_flag; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait_bounded(&k_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
-        mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sK + s * TILE_BYTES + h * HALF_BYTES, &tmK, &k_full[s], h * 64, j * BKV, bh);
+        mbar_arrive_expect_tx(&k_full[s], tile_bytes<HD>());
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sK + s * tile_bytes<HD>() + h * BOX_BYTES, &tmK, &k_full[s], h * 64, j * BKV, bh);
         FMHA_TRACE(13, j);
         if (!mbar_wait_bounded(&v_empty[s], ph ^ 1, abort_flag, ERR_BIT)) break;
-        mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sV + s * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[s], h * 64, j * BKV, bh);
+        mbar_arrive_expect_tx(&v_full[s], tile_bytes<HD>());
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sV + s * tile_bytes<HD>() + h * BOX_BYTES, &tmV, &v_full[s], h * 64, j * BKV, bh);
         FMHA_TRACE(14, j);
       }
     }
@@ -509,8 +516,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[0], 0, abort_flag, ERR_BIT));
       if (ok) {
         tc_fence_after();
-        issue_s(tmem, sQa, sKa, 0, 0, &s_full[0]);
-        issue_s(tmem, sQa, sKa, 1, 0, &s_full[1]);
+        issue_s<HD>(tmem, sQa, sKa, 0, 0, &s_full[0]);
+        issue_s<HD>(tmem, sQa, sKa, 1, 0, &s_full[1]);
         mma_commit_elect(&k_empty[0]);
       }
       // Tensor-pipe order per key block j: PV0(j) S0(j+1) PV1(j) S1(j+1). The
@@ -527,7 +534,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int q = 0; q < P_PARTS && ok; ++q) {
             if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[q], j & 1, abort_flag, ERR_BIT)))) break;
             tc_fence_after();
-            issue_pv(tmem, sVa, 0, s, j, q, lane == 0 && j == 30);
+            issue_pv<HD>(tmem, sVa, 0, s, j, q, lane == 0 && j == 30);
           }
           if (!ok) break;
           if (j + 1 == nb0 && nb0 < nb) mma_commit_elect(&o_full[0]);  // tile 0 done early
@@ -539,7 +546,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (more) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&k_full[sn], phn, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
-          if (j + 1 < nb0) issue_s(tmem, sQa, sKa, 0, sn, &s_full[0], lane == 0 && j == 30);
+          if (j + 1 < nb0) issue_s<HD>(tmem, sQa, sKa, 0, sn, &s_full[0], lane == 0 && j == 30);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[1]);
 #endif
@@ -548,7 +555,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int q = 0; q < P_PARTS && ok; ++q) {
           if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_full[P_PARTS + q], j & 1, abort_flag, ERR_BIT)))) break;
           tc_fence_after();
-          issue_pv(tmem, sVa, 1, s, j, q, lane == 0 && j == 30);
+          issue_pv<HD>(tmem, sVa, 1, s, j, q, lane == 0 && j == 30);
         }
         if (!ok) break;
 #ifdef CTB_FMHA_TRACE
@@ -557,7 +564,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) FMHA_TRACE(5, j);
         mma_commit_elect(&v_empty[s]);
         if (more) {
-          issue_s(tmem, sQa, sKa, 1, sn, &s_full[1], lane == 0 && j == 30);
+          issue_s<HD>(tmem, sQa, sKa, 1, sn, &s_full[1], lane == 0 && j == 30);
 #ifdef CTB_FMHA_TRACE
         mma_commit_elect(&grp_done[3]);
 #endif
@@ -587,9 +594,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;   // TMEM lanes 32*quarter .. +31
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + lane_off + t * BKV;
-    const uint32_t o_col = tmem + lane_off + 256 + t * D;
+    const uint32_t o_col = tmem + lane_off + 256 + t * HD;
     const int qrow = q0 + t * BQ + quarter * 32 + lane;
-    softmax_rows(p, t, s_col, o_col, qrow, q0 + t * BQ, bh, t == 0 ? nb0 : nb, &s_full[t], &o_full[t], abort_flag,
+    softmax_rows<HD>(p, t, s_col, o_col, qrow, q0 + t * BQ, bh, t == 0 ? nb0 : nb, &s_full[t], &o_full[t], abort_flag,
                  [&](int part) { mbar_arrive(&p_full[t * P_PARTS + part]); });
   }
 
@@ -821,7 +828,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row0 = q0 + t * 2 * BQ + rank * BQ;
     const int qrow = row0 + quarter * 32 + lane;
     const uint32_t p_bar = mapa_shared(smem_u32(&p_full[t * P_PARTS]), 0);
-    softmax_rows(p, t, s_col, o_col, qrow, row0, bh, nbt[t], &s_full[t], &o_full[t], abort_flag,
+    softmax_rows<D>(p, t, s_col, o_col, qrow, row0, bh, nbt[t], &s_full[t], &o_full[t], abort_flag,
                  [&](int part) {
                    __syncwarp();
                    if (lane == 0) mbar_arrive_cluster(p_bar + 8 * part);
@@ -882,9 +889,12 @@ int fmha_device_setup() {
   unsigned long long ctx = 0;
   if (int rc = current_context_id(&ctx)) return rc;
   if (dev < 64 && g_fmha_attr_done[dev] == ctx) return CTB_OK;
-  CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_tcgen05_kernel,
+  CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_tcgen05_kernel<128>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      fmha::SMEM_BYTES));
+                                      fmha::smem_bytes<128>()));
+  CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_tcgen05_kernel<64>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      fmha::smem_bytes<64>()));
   CTB_CUDA_CHECK(cudaFuncSetAttribute(fmha::fmha_fwd_pair_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       fmha::PR_SMEM_BYTES));
@@ -917,23 +927,23 @@ static bool fmha_use_pair() {
 }
 
 static int fmha_tc(const __half* Q, const __half* K, const __half* V, __half* O, int B, int H,
-                   int Sq, int Sk, float scale, int causal, cudaStream_t st) {
+                   int Sq, int Sk, int hd, float scale, int causal, cudaStream_t st) {
   if (int rc = fmha_device_setup()) return rc;
   const int BH = B * H;
-  const bool pair = fmha_use_pair();
+  const bool pair = hd == fmha::D && fmha_use_pair();
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, 128, 1};
   const uint32_t kbox[3] = {64, pair ? 64u : 128u, 1};  // a CTA of a pair loads 64 keys
   {
-    const uint64_t dims[3] = {(uint64_t)fmha::D, (uint64_t)Sq, (uint64_t)BH};
-    const uint64_t strides[2] = {(uint64_t)fmha::D * 2, (uint64_t)Sq * fmha::D * 2};
+    const uint64_t dims[3] = {(uint64_t)hd, (uint64_t)Sq, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)hd * 2, (uint64_t)Sq * hd * 2};
     if (int rc = encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, Q, dims, strides, box,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
   {
-    const uint64_t dims[3] = {(uint64_t)fmha::D, (uint64_t)Sk, (uint64_t)BH};
-    const uint64_t strides[2] = {(uint64_t)fmha::D * 2, (uint64_t)Sk * fmha::D * 2};
+    const uint64_t dims[3] = {(uint64_t)hd, (uint64_t)Sk, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)hd * 2, (uint64_t)Sk * hd * 2};
     if (int rc = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, K, dims, strides, kbox,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
@@ -960,8 +970,12 @@ static int fmha_tc(const __half* Q, const __half* K, const __half* V, __half* O,
   }
   const int64_t grid = (int64_t)p.n_qblk * BH;
   if (grid > 0x7fffffff) return set_error(CTB_ERR_SHAPE, "fmha: too many query blocks");
-  fmha::fmha_fwd_tcgen05_kernel<<<(unsigned)grid, fmha::THREADS, fmha::SMEM_BYTES, st>>>(tq, tk,
-                                                                                         tv, p);
+  if (hd == 64)
+    fmha::fmha_fwd_tcgen05_kernel<64>
+        <<<(unsigned)grid, fmha::THREADS, fmha::smem_bytes<64>(), st>>>(tq, tk, tv, p);
+  else
+    fmha::fmha_fwd_tcgen05_kernel<128>
+        <<<(unsigned)grid, fmha::THREADS, fmha::smem_bytes<128>(), st>>>(tq, tk, tv, p);
   return launch_status("fmha_fwd_tcgen05_kernel");
 }
 
@@ -981,11 +995,11 @@ extern "C" int ctb_fmha_fwd_f16(const void* Q, const void* K, const void* V, voi
   DeviceProps p;
   if (int rc = current_props(&p)) return rc;
   auto st = static_cast<cudaStream_t>(stream);
-  const bool tc_ok = head_dim == fmha::D && aligned16(Q) && aligned16(K) && aligned16(V) &&
+  const bool tc_ok = (head_dim == 128 || head_dim == 64) && aligned16(Q) && aligned16(K) && aligned16(V) &&
                      aligned16(O) && (int64_t)batch * heads <= 0x7fffffff;
   if (tc_ok)
     return fmha_tc((const __half*)Q, (const __half*)K, (const __half*)V, (__half*)O, batch, heads,
-                   seq_q, seq_k, scale, causal ? 1 : 0, st);
+                   seq_q, seq_k, head_dim, scale, causal ? 1 : 0, st);
   return fmha_simt((const __half*)Q, (const __half*)K, (const __half*)V, (__half*)O, batch, heads,
                    seq_q, seq_k, head_dim, scale, causal ? 1 : 0, st);
 }

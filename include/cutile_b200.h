@@ -224,7 +224,9 @@ int ctb_bgemm_f16(const void* A, const void* B, void* C, int32_t M, int32_t N,
 /* Attention forward, Float16 Q/K/V/O, Float32 softmax accumulation:
  * O[b,h] = softmax(scale * Q K^T [+ causal mask: key j > query i masked]) V.
  * Layout row-major [batch, heads, seq, head_dim] (= Julia (D, S, H, B),
- * head_dim contiguous). head_dim must be 64 or 128. cuTile example
+ * head_dim contiguous). head_dim must be 64 or 128; both run on the tcgen05
+ * tensor-core kernel when the four pointers are 16-byte aligned (a CUDA-core
+ * kernel serves unaligned pointers). cuTile example
  * fmha.jl:20 (not vendored; report.html:2981). */
 int ctb_fmha_fwd_f16(const void* Q, const void* K, const void* V, void* O,
                      int32_t batch, int32_t heads, int32_t seq_q,

@@ -300,7 +300,8 @@ def fmha_case(dev, B, H, S, D, causal, seed, rows=None, pairs=None):
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("B,H,S,D", [(1, 2, 128, 128), (2, 2, 256, 64), (1, 1, 1000, 128),
                                      (1, 2, 1024, 128), (1, 1, 77, 64), (2, 1, 600, 128),
-                                     (1, 1, 1536, 128), (1, 1, 200, 128)])
+                                     (1, 1, 1536, 128), (1, 1, 200, 128), (1, 2, 1024, 64),
+                                     (2, 1, 1000, 64), (1, 1, 1536, 64)])
 def test_fmha(dev, B, H, S, D, causal):
     fmha_case(dev, B, H, S, D, causal, 50)
 
