@@ -111,7 +111,8 @@ def test_rowsum_generic_strides(dev):
 
 # ----------------------------------------------------------------------------- softmax
 @pytest.mark.parametrize("count,length", [(2048, 1000), (4096, 16384), (17, 1), (9, 3),
-                                          (33, 4097), (5, 32768), (3, 40000), (64, 513)])
+                                          (33, 4097), (5, 32768), (3, 40000), (64, 513),
+                                          (512, 16384), (300, 12000), (1, 16384), (149, 8196)])
 def test_softmax(dev, count, length):
     x = N((count, length), 7, dev, std=4.0)
     y = ops.softmax(x)
