@@ -8,6 +8,7 @@
 #include "ctb_common.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace ctb {
 
@@ -106,11 +107,17 @@ static int launch_vadd(const T* a, const T* b, T* c, int64_t n, int64_t sa, int6
 // =============================================================================
 // Julia column-major a (s_i == 1): consecutive threads own consecutive rows
 // (one float4 = 4 rows each), RS_Y thread rows split the j range, shared
-// memory folds the RS_Y partial sums.
-constexpr int RS_X = 64, RS_Y = 8;  // 64 x 4 = 256 rows per CTA, 512 threads
-__global__ void __launch_bounds__(RS_X* RS_Y) rowsum_rows_contig_kernel(
+// memory folds the RS_Y partial sums. A CTA of 512 threads covers RS_X x 4
+// rows; the launcher takes the widest RS_X (64, 32, 16, 8) that still gives
+// two CTAs per SM, so a short matrix (a shard of the job) spreads over every
+// SM. Measured (B200, m x 512, GB/s): m = 131072: RS_X 64 6003, 32 5978, 16
+// 5781; m = 65536: 4950 / 5301 / 5083; m = 32768: 2963 / 3793 / 4054;
+// m = 16384: 1521 / 2314 / 2714.
+template <int RS_X>
+__global__ void __launch_bounds__(512) rowsum_rows_contig_kernel(
     const float* __restrict__ a, float* __restrict__ out, int m, int n, int64_t sj,
     int64_t so) {
+  constexpr int RS_Y = 512 / RS_X;
   __shared__ float4 part[RS_Y][RS_X];
   const int tx = threadIdx.x % RS_X, ty = threadIdx.x / RS_X;
   const int64_t row0 = (int64_t)blockIdx.x * (RS_X * 4) + tx * 4;
@@ -201,8 +208,15 @@ static int launch_rowsum(const float* a, float* out, int m, int n, int64_t si, i
   if (int rc = current_props(&p)) return rc;
   if (m == 0) return CTB_OK;
   if (si == 1 && m % 4 == 0 && sj % 4 == 0 && aligned16(a)) {
-    const int grid = (m + RS_X * 4 - 1) / (RS_X * 4);
-    rowsum_rows_contig_kernel<<<grid, RS_X * RS_Y, 0, st>>>(a, out, m, n, sj, so);
+    auto go = [&](auto rsx) {
+      constexpr int X = decltype(rsx)::value;
+      rowsum_rows_contig_kernel<X><<<(m + X * 4 - 1) / (X * 4), 512, 0, st>>>(a, out, m, n, sj, so);
+    };
+    const int64_t want = 2 * (int64_t)p.sm_count;  // CTAs
+    if ((m + 255) / 256 >= want) go(std::integral_constant<int, 64>{});
+    else if ((m + 127) / 128 >= want) go(std::integral_constant<int, 32>{});
+    else if ((m + 63) / 64 >= want) go(std::integral_constant<int, 16>{});
+    else go(std::integral_constant<int, 8>{});
     return launch_status("rowsum_rows_contig_kernel");
   }
   if (sj == 1) {

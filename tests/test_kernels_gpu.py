@@ -88,7 +88,8 @@ def test_vadd_full_size(dev):
 
 
 # ----------------------------------------------------------------------------- rowsum
-@pytest.mark.parametrize("m,n", [(4096, 128), (131072, 512), (1000, 33), (4100, 7), (3, 1)])
+@pytest.mark.parametrize("m,n", [(4096, 128), (131072, 512), (1000, 33), (4100, 7), (3, 1),
+                                 (65536, 512), (32768, 300), (16384, 512)])
 def test_rowsum_julia_colmajor(dev, m, n):
     a = N((n, m), 4, dev)  # Julia m x n, stride (1, m)
     out = ops.rowsum(a)
