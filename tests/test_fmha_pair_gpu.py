@@ -27,13 +27,15 @@ out = []
 def randn(shape, seed):
     g = torch.Generator(device="cpu").manual_seed(seed)
     return torch.randn(shape, generator=g).to(torch.float16).to(dev)
-for (B, H, S, causal, ramp) in [(1, 1, 512, False, False), (1, 1, 512, True, False),
-                                (1, 2, 1024, True, False), (2, 1, 600, False, False),
-                                (1, 1, 1000, True, False), (1, 1, 77, True, False),
-                                (1, 2, 1536, False, False), (1, 1, 1024, True, True)]:
-    q, k, v = randn((B, H, S, 128), 1), randn((B, H, S, 128), 2), randn((B, H, S, 128), 3)
+for (B, H, S, Sk, causal, ramp) in [(1, 1, 512, 512, False, False), (1, 1, 512, 512, True, False),
+                                    (1, 2, 1024, 1024, True, False), (2, 1, 600, 600, False, False),
+                                    (1, 1, 1000, 1000, True, False), (1, 1, 77, 77, True, False),
+                                    (1, 2, 1536, 1536, False, False), (1, 1, 1024, 1024, True, True),
+                                    (1, 1, 300, 1000, True, False), (1, 1, 1000, 300, True, False),
+                                    (1, 1, 700, 129, False, False)]:
+    q, k, v = randn((B, H, S, 128), 1), randn((B, H, Sk, 128), 2), randn((B, H, Sk, 128), 3)
     if ramp:  # scores grow along the keys: the running max moves many times
-        k = (k * torch.linspace(0.2, 6.0, S, device=dev, dtype=torch.float16).view(1, 1, S, 1)).contiguous()
+        k = (k * torch.linspace(0.2, 6.0, Sk, device=dev, dtype=torch.float16).view(1, 1, S, 1)).contiguous()
         q = (torch.ones_like(q) * torch.sign(k.sum(dim=2, keepdim=True))).contiguous()
     o = ops.fmha(q, k, v, 1.0 / math.sqrt(128), causal)
     torch.cuda.synchronize()
@@ -44,7 +46,7 @@ for (B, H, S, causal, ramp) in [(1, 1, 512, False, False), (1, 1, 512, True, Fal
         for h in range(H):
             ref = O.fmha(hq[b, h], hk[b, h], hv[b, h], 1.0 / math.sqrt(128), causal)
             ok = ok and bool(np.all(np.isfinite(ho[b, h]))) and bool(O.isapprox(ho[b, h], ref, 1e-2))
-    out.append([B, H, S, causal, ramp, ok])
+    out.append([B, H, S, Sk, causal, ramp, ok])
 print(json.dumps(out))
 """
 
@@ -55,6 +57,6 @@ def test_pair_kernel_parity():
                        text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     rows = json.loads(r.stdout.strip().splitlines()[-1])
-    assert len(rows) == 8
-    for B, H, S, causal, ramp, ok in rows:
-        assert ok, (B, H, S, causal, ramp)
+    assert len(rows) == 11
+    for B, H, S, Sk, causal, ramp, ok in rows:
+        assert ok, (B, H, S, Sk, causal, ramp)

@@ -309,6 +309,25 @@ def test_fmha(dev, B, H, S, D, causal):
 
 
 @pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("Sq,Sk", [(300, 1000), (1000, 300), (129, 77), (512, 2048), (2048, 129)])
+def test_fmha_cross_lengths(dev, Sq, Sk, D, causal):
+    """seq_q != seq_k (the ABI's separate lengths): ragged key blocks, query
+    blocks past the last key, and causal masks that end inside a key block."""
+    q = N((1, 2, Sq, D), 80, dev, torch.float16)
+    k = N((1, 2, Sk, D), 81, dev, torch.float16)
+    v = N((1, 2, Sk, D), 82, dev, torch.float16)
+    scale = 1.0 / math.sqrt(D)
+    o = ops.fmha(q, k, v, scale, causal)
+    ops.check_device()
+    hq, hk, hv, ho = host(q), host(k), host(v), host(o)
+    for h in range(2):
+        ref = O.fmha(hq[0, h], hk[0, h], hv[0, h], scale, causal)
+        assert np.all(np.isfinite(ho[0, h]))
+        assert O.isapprox(ho[0, h], ref, 1e-2), h
+
+
+@pytest.mark.parametrize("causal", [False, True])
 def test_fmha_running_max_grows(dev, causal):
     """Scores that grow along the key axis force the running max up by more
     than the rescale threshold many times (the O rescale and exponential-redo
